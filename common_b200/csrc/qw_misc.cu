@@ -1,0 +1,135 @@
+// qw_misc.cu -- weight placement / conversion, synthetic initialisation, RoPE table, and the
+// small reductions used around the tensor-parallel collectives.
+#include "qw_internal.cuh"
+#include "qw_kernels.h"
+#include <float.h>
+#include <limits.h>
+
+namespace qw {
+
+// dst[map(r) * ld + c] = convert(src[r * src_ld + c])  or the synthetic value of the full
+// tensor's element (src_row0 + r, src_col0 + c).
+template <typename DT>
+__global__ void place_kernel(const PlaceArgs p) {
+    const size_t total = (size_t)p.rows * p.cols;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        int r = (int)(i / p.cols), c = (int)(i % p.cols);
+        float v;
+        if (p.synth) {
+            size_t gidx = (size_t)(p.src_row0 + r) * p.full_cols + (p.src_col0 + c);
+            v = p.constant_one ? 1.0f : synth_value(p.seed, p.tensor_id, gidx, p.scale);
+        } else {
+            size_t s = (size_t)r * p.src_ld + c;
+            if (p.src_dtype == 0) v = reinterpret_cast<const float *>(p.src)[s];
+            else if (p.src_dtype == 1) v = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(p.src)[s] << 16);
+            else v = (float)reinterpret_cast<const double *>(p.src)[s];
+        }
+        int dr;
+        if (p.row_map == 0) dr = p.dst_row0 + r;
+        else {
+            int blk = r / kGuBlock, w = r % kGuBlock;
+            dr = blk * 2 * kGuBlock + (p.row_map == 2 ? kGuBlock : 0) + w;
+        }
+        Elt<DT>::store(reinterpret_cast<DT *>(p.dst) + (size_t)dr * p.dst_ld + c, v);
+    }
+}
+
+cudaError_t place_launch(const PlaceArgs &p, cudaStream_t st) {
+    size_t total = (size_t)p.rows * p.cols;
+    if (!total) return cudaSuccess;
+    int grid = (int)((total + 255) / 256);
+    if (grid > 148 * 16) grid = 148 * 16;
+    if (p.dst_bf16) place_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else place_kernel<float><<<grid, 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+// freq[p][f] = (cos, sin)(p * exp(-2 f ln(theta) / d)), computed in fp64 like the reference's
+// default precision (RotationFeatures.java:189-208), stored as fp32.
+__global__ void freq_kernel(float2 *freq, int seq_len, int half, double neg2lt_over_d) {
+    size_t total = (size_t)seq_len * half;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        int p = (int)(i / half), f = (int)(i % half);
+        double inv = exp((double)f * neg2lt_over_d);
+        double ang = (double)p * inv;
+        freq[i] = make_float2((float)cos(ang), (float)sin(ang));
+    }
+}
+
+cudaError_t freq_launch(float2 *freq, int seq_len, int head_dim, double theta, cudaStream_t st) {
+    int half = head_dim / 2;
+    size_t total = (size_t)seq_len * half;
+    int grid = (int)((total + 255) / 256);
+    if (grid > 148 * 8) grid = 148 * 8;
+    freq_kernel<<<grid, 256, 0, st>>>(freq, seq_len, half, -2.0 * log(theta) / head_dim);
+    return cudaGetLastError();
+}
+
+// Cross-rank greedy pick: (val, idx) gathered from every rank -> winner (ties -> smaller index).
+__global__ void argmax_merge_kernel(const float *vals, const int *idxs, int tp, int B, int *argmax_out,
+                                    int *next_tokens, int *positions, int advance, int *hist, int hist_ld) {
+    int b = threadIdx.x;
+    if (b >= B) return;
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int r = 0; r < tp; r++) {
+        float v = vals[r * B + b];
+        int i = idxs[r * B + b];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    if (argmax_out) argmax_out[b] = bi;
+    if (hist) hist[(size_t)b * hist_ld + positions[b] + 1] = bi;
+    if (advance) {
+        next_tokens[b] = bi;
+        positions[b] += 1;
+    }
+}
+
+cudaError_t argmax_merge_launch(const float *vals, const int *idxs, int tp, int B, int *argmax_out, int *next_tokens,
+                                int *positions, int advance, int *hist, int hist_ld, cudaStream_t st) {
+    argmax_merge_kernel<<<1, 32 * ((B + 31) / 32), 0, st>>>(vals, idxs, tp, B, argmax_out, next_tokens, positions, advance,
+                                                            hist, hist_ld);
+    return cudaGetLastError();
+}
+
+// Per-rank sums of squares of the local q and k slices (whole-vector QK-norm under tensor
+// parallelism; the caller all-reduces them).  out: (B, 2).
+__global__ void qk_sumsq_kernel(const float *qkv, int ld, int qw, int kw, float *out) {
+    int b = blockIdx.x;
+    const float *row = qkv + (size_t)b * ld;
+    float sq = 0.f, sk = 0.f;
+    for (int i = threadIdx.x; i < qw; i += blockDim.x) sq += row[i] * row[i];
+    for (int i = threadIdx.x; i < kw; i += blockDim.x) sk += row[qw + i] * row[qw + i];
+    __shared__ float s[2][32];
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) { s[0][w] = sq; s[1][w] = sk; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.f, c = 0.f;
+        for (int i = 0; i < (int)(blockDim.x / 32); i++) { a += s[0][i]; c += s[1][i]; }
+        out[b * 2 + 0] = a;
+        out[b * 2 + 1] = c;
+    }
+}
+
+cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, float *out, cudaStream_t st) {
+    qk_sumsq_kernel<<<B, 256, 0, st>>>(qkv, ld, qw, kw, out);
+    return cudaGetLastError();
+}
+
+// x_out = x_in + part (residual after a tensor-parallel all-reduce), rows x n
+__global__ void add_kernel(float *out, const float *a, const float *b, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = a[i] + b[i];
+}
+cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cudaStream_t st) {
+    int grid = (int)((n + 255) / 256);
+    if (grid > 148 * 8) grid = 148 * 8;
+    if (grid < 1) grid = 1;
+    add_kernel<<<grid, 256, 0, st>>>(out, a, b, n);
+    return cudaGetLastError();
+}
+
+}  // namespace qw

@@ -1,0 +1,207 @@
+/*
+ * qwen3_b200.h -- C ABI of libqwen3_b200.so, the B200 (sm_100a) backend for the
+ * almostrealism/common Qwen3 forward step.
+ *
+ * The reference runs this step as a Java operation graph (engine/ml Qwen3 ->
+ * CompiledModel) lowered to generated C kernels that are entered through JNI, one
+ * kernel per graph node:
+ *   JNIEXPORT void JNICALL Java_<GeneratedOperationN>_apply(JNIEnv*, jobject, jlong commandQueue,
+ *       jlongArray arg, jintArray offset, jintArray size, jint count, jint globalId, jlong kernelSize)
+ *   (base/hardware/src/main/resources/.../generated.javatemplate:21-25,
+ *    base/hardware/src/main/java/org/almostrealism/hardware/jni/NativeInstructionSet.java:39-121)
+ * This library replaces the whole compiled model rather than individual graph nodes:
+ * one call runs the full forward step of every layer.  Each entry point below names
+ * the reference call it stands in for.
+ *
+ * Conventions
+ *   - plain C types only; every function returns qw_status (0 = OK);
+ *   - host buffers are borrowed for the duration of the call, never retained;
+ *   - the library owns all device memory it allocates;
+ *   - calls on one qw_model must be serialised by the caller (the reference's
+ *     AutoregressiveModel is single-threaded as well);
+ *   - one CUDA stream per model; `*_device` entry points take device pointers and
+ *     enqueue on that stream without synchronising.
+ */
+#ifndef QWEN3_B200_H
+#define QWEN3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QW_ABI_VERSION 1
+
+typedef int32_t qw_status;
+enum {
+    QW_OK = 0,
+    QW_ERR_ARG = 1,         /* null pointer / bad argument (reference: NullPointerException) */
+    QW_ERR_SHAPE = 2,       /* tensor or batch shape mismatch (IllegalArgumentException) */
+    QW_ERR_OOM = 3,         /* device allocation failed */
+    QW_ERR_CUDA = 4,        /* CUDA runtime error */
+    QW_ERR_NCCL = 5,        /* NCCL error */
+    QW_ERR_TIMEOUT = 6,     /* a bounded device wait gave up */
+    QW_ERR_STATE = 7,       /* call not valid in this state (e.g. weights not finalized) */
+    QW_ERR_UNSUPPORTED = 8, /* configuration not supported by this build */
+    QW_ERR_KEY = 9          /* unknown state-dict key */
+};
+
+typedef enum { QW_DTYPE_F32 = 0, QW_DTYPE_BF16 = 1, QW_DTYPE_F64 = 2 } qw_dtype;
+
+/* QK-norm variants.  QW_QKNORM_VECTOR is the reference's behaviour: rmsnorm over the
+ * whole projected q (and k) vector with the (heads, head_dim) weight flattened
+ * (engine/ml/src/main/java/org/almostrealism/ml/AttentionFeatures.java:840-845, 886-891).
+ * QW_QKNORM_HEAD normalises each head over head_dim (HuggingFace Qwen3). */
+typedef enum { QW_QKNORM_NONE = 0, QW_QKNORM_VECTOR = 1, QW_QKNORM_HEAD = 2 } qw_qknorm;
+
+/* Model geometry: engine/ml/src/main/java/org/almostrealism/ml/qwen3/Qwen3Config.java:574-588 and
+ * TransformerConfig.java:94-105.  head_dim is explicit (the reference derives dim/heads,
+ * TransformerConfig.java:104); heads*head_dim may differ from dim. */
+typedef struct qw_config {
+    int32_t dim;            /* hidden size */
+    int32_t hidden_dim;     /* SwiGLU intermediate size */
+    int32_t layers;
+    int32_t heads;
+    int32_t kv_heads;
+    int32_t head_dim;       /* 64 or 128 */
+    int32_t vocab;
+    int32_t seq_len;        /* max positions per sequence slot (reference seqLen) */
+    int32_t shared_weights; /* lm_head tied to model.embed_tokens.weight */
+    int32_t qk_norm;        /* qw_qknorm */
+    int32_t has_qkv_bias;   /* q/k/v projection biases (Qwen2.5 layout) */
+    int32_t weight_dtype;   /* QW_DTYPE_F32 or QW_DTYPE_BF16: storage and GEMV input type */
+    int32_t kv_dtype;       /* QW_DTYPE_F32 or QW_DTYPE_BF16 */
+    int32_t max_batch;      /* sequence slots */
+    int32_t max_tokens;     /* max tokens in one prefill call (activation arena), >= max_batch */
+    int32_t page_size;      /* KV page size in tokens (power of two, 16..256); 0 = 64 */
+    int32_t num_pages;      /* KV pages per rank; 0 = max_batch * ceil(seq_len / page_size) */
+    int32_t reserved[5];
+    double rope_theta;      /* 1e6 for Qwen3 */
+    double eps;             /* rmsnorm epsilon, 1e-6 for Qwen3 */
+} qw_config;
+
+typedef struct qw_model qw_model;
+
+/* Library version / build information ("sm_100a", ABI version). */
+int32_t qw_abi_version(void);
+const char *qw_build_info(void);
+
+/* NCCL unique id (128 bytes) for tensor-parallel creation; call on rank 0 and share. */
+qw_status qw_get_unique_id(void *out128);
+
+/* Create a model on `device`.  tp_size > 1 shards every layer Megatron-style over
+ * tp_size ranks (one process per GPU) and joins the NCCL communicator named by
+ * nccl_unique_id.  Stands in for the Qwen3 constructor
+ * (engine/ml/src/main/java/org/almostrealism/ml/qwen3/Qwen3.java:249-255). */
+qw_status qw_create(const qw_config *cfg, int32_t device, int32_t tp_rank, int32_t tp_size,
+                    const void *nccl_unique_id, qw_model **out);
+
+/* Copy one state-dict tensor (HF key, Qwen3.java:361-382) from host memory.  The
+ * rank keeps only its shard.  Accepts F32, BF16 or F64 host data and converts to the
+ * configured storage type.  Stands in for StateDictionary.get
+ * (engine/ml/src/main/java/org/almostrealism/ml/StateDictionary.java:119-150). */
+qw_status qw_load_tensor(qw_model *m, const char *key, qw_dtype dtype, const int64_t *dims,
+                         int32_t ndims, const void *host_ptr);
+
+/* Fill every weight on the device from the counter-based synthetic generator
+ * (seed, std); all rmsnorm / q_norm / k_norm weights are set to 1. */
+qw_status qw_init_synthetic(qw_model *m, uint64_t seed, float std);
+
+/* Validate that every required tensor is present and build fused layouts. */
+qw_status qw_finalize_weights(qw_model *m);
+
+/* Clear a sequence slot (-1 = all): frees its KV pages and zeroes its length.
+ * Stands in for CompiledModel.reset / AutoregressiveModel.reset
+ * (domain/graph/src/main/java/org/almostrealism/model/CompiledModel.java:218-220). */
+qw_status qw_reset(qw_model *m, int32_t slot);
+
+/* Make sure slot `slot` has KV pages for positions [0, n_positions). */
+qw_status qw_reserve(qw_model *m, int32_t slot, int32_t n_positions);
+
+/* One forward step for `batch` sequences, one token each: token[b] at position
+ * positions[b] of slot slots[b] (slots may be NULL = 0..batch-1).  Writes logits
+ * (batch x vocab, fp32, may be NULL) and the greedy token (first index of the max,
+ * AggregationFeatures.java:111-121; may be NULL).  Stands in for
+ * CompiledModel.forward + indexOfMax (CompiledModel.java:189-198,
+ * engine/ml/src/main/java/org/almostrealism/ml/AutoregressiveModel.java:295-308, 412-420). */
+qw_status qw_decode_step(qw_model *m, const int32_t *tokens, const int32_t *slots,
+                         const int32_t *positions, int32_t batch, float *logits_out,
+                         int32_t *argmax_out);
+
+/* Same as qw_decode_step with an embedding row supplied instead of a token id:
+ * x_in is (batch, dim) fp32 -- CompiledModel.forward((1, dim)) exactly. */
+qw_status qw_forward_hidden(qw_model *m, const float *x_in, const int32_t *slots,
+                            const int32_t *positions, int32_t batch, float *logits_out,
+                            int32_t *argmax_out);
+
+/* Process `batch` prompts of `seq_len` tokens each (tokens row-major batch x seq_len)
+ * into slots (NULL = 0..batch-1) starting at position 0.  Writes the logits / greedy
+ * token of each prompt's last position (either may be NULL).  The reference has no
+ * batched prefill (it feeds prompt tokens one per forward, AutoregressiveModel.java:296-299);
+ * results equal feeding the tokens one by one, within the bf16 tolerance. */
+qw_status qw_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, int32_t batch,
+                     int32_t seq_len, float *logits_out, int32_t *argmax_out);
+
+/* Greedy autoregressive generation (AutoregressiveModel.next loop,
+ * AutoregressiveModel.java:295-308): prompts (batch x prompt_len) are fed first,
+ * then each step feeds the argmax of the previous step's logits.  tokens_out
+ * (batch x steps) receives the token fed at every step (prompt tokens included),
+ * i.e. what next() returns.  steps >= prompt_len. */
+qw_status qw_generate(qw_model *m, const int32_t *prompts, int32_t batch, int32_t prompt_len,
+                      int32_t steps, int32_t *tokens_out);
+
+/* Device-resident variant of qw_decode_step for benchmarking and graph replay:
+ * all pointers are device pointers; enqueued on the model's stream.  Pages must
+ * already be reserved (qw_reserve).  If advance != 0 the kernel writes the argmax
+ * into d_tokens and increments d_positions, so repeated calls run greedy decode
+ * with no host involvement. */
+qw_status qw_decode_step_device(qw_model *m, int32_t *d_tokens, const int32_t *d_slots,
+                                int32_t *d_positions, int32_t batch, float *d_logits,
+                                int32_t *d_argmax, int32_t advance);
+
+/* Capture the device decode step for `batch` into a CUDA graph (replayed by
+ * qw_replay_decode) -- pointers as for qw_decode_step_device. */
+qw_status qw_capture_decode(qw_model *m, int32_t *d_tokens, const int32_t *d_slots,
+                            int32_t *d_positions, int32_t batch, float *d_logits, int32_t *d_argmax);
+qw_status qw_replay_decode(qw_model *m, int32_t times);
+
+/* Kernel classes reported by qw_profile_decode. */
+enum {
+    QW_KERNEL_OTHER = 0,
+    QW_KERNEL_QKV = 1,     /* rmsnorm + fused q/k/v projection */
+    QW_KERNEL_ATTN = 2,    /* QK-norm + RoPE + KV write + paged attention */
+    QW_KERNEL_O = 3,       /* o projection + residual */
+    QW_KERNEL_GATE_UP = 4, /* rmsnorm + gate/up projection + SwiGLU */
+    QW_KERNEL_DOWN = 5,    /* down projection + residual */
+    QW_KERNEL_LM_HEAD = 6  /* final rmsnorm + lm_head + argmax */
+};
+
+/* Set the device-side token / position of sequences 0..batch-1 (slots 0..batch-1) used by
+ * qw_profile_decode, reserving KV pages. */
+qw_status qw_set_device_inputs(qw_model *m, const int32_t *tokens, const int32_t *positions, int32_t batch);
+
+/* Run one eager decode step on the model's own device inputs (qw_set_device_inputs) with
+ * CUDA events around every kernel launch; writes up to `cap` launch durations (ms) and
+ * their QW_KERNEL_* classes, and the launch count to *n_out.  Does not advance positions. */
+qw_status qw_profile_decode(qw_model *m, int32_t batch, float *ms_out, int32_t *kinds_out, int32_t cap,
+                            int32_t *n_out);
+
+/* Wait for all work on the model's stream. */
+qw_status qw_synchronize(qw_model *m);
+
+/* The model's CUDA stream (cudaStream_t) for event timing by the caller. */
+void *qw_stream(qw_model *m);
+
+/* Number of kernel launches the last decode step / prefill enqueued. */
+int32_t qw_last_launch_count(const qw_model *m);
+
+/* Human-readable description of the last error on this model (never NULL). */
+const char *qw_last_error(const qw_model *m);
+
+void qw_destroy(qw_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
