@@ -264,13 +264,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
 // ---------------------------------------------------------------------------------------------
 // launcher
 // ---------------------------------------------------------------------------------------------
-// blocks per SM for (kernel, dynamic smem), cached: queried outside of stream capture on first use
-static int occupancy_cached(const void *fn, size_t smem) {
+// Opt the kernel in to `smem` bytes of dynamic shared memory and return its blocks per SM;
+// cached per (kernel, smem) so the attribute calls happen once, outside of stream capture.
+static int prepare_cached(const void *fn, size_t smem, cudaError_t *err) {
     static std::mutex mu;
     static std::map<std::pair<const void *, size_t>, int> cache;
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find({fn, smem});
     if (it != cache.end()) return it->second;
+    *err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (*err != cudaSuccess) return 0;
     int occ = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kGemvThreads, smem) != cudaSuccess || occ < 1) occ = 1;
     cache[{fn, smem}] = occ;
@@ -281,11 +284,9 @@ template <typename WT, int EPI, int NB>
 static cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t st) {
     size_t smem = (size_t)NB * a.K * sizeof(float);
     auto kfn = gemv_kernel<WT, EPI, NB>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    int occ = occupancy_cached((const void *)kfn, smem);
+    cudaError_t e = cudaSuccess;
+    int occ = prepare_cached((const void *)kfn, smem, &e);
+    if (e != cudaSuccess) return e;
     int ntask = (EPI == EPI_SWIGLU) ? a.N / 2 : (a.N + 1) / 2;
     int want = (ntask + (kGemvThreads / 32) - 1) / (kGemvThreads / 32);
     int cap = num_sms * occ;
