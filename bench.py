@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 
 GEOM_8B = dict(dim=4096, hidden_dim=12288, layers=36, heads=32, kv_heads=8, head_dim=128, vocab=151936,
                shared_weights=0, qk_norm=1, has_qkv_bias=0, rope_theta=1e6, eps=1e-6)
-PROMPT = 512
+PROMPT = 512  # default prompt length (--prompt-len)
 METRIC = "Qwen3-8B decode tok/s (batch 1, bf16, 512-token prompt)"
 
 
@@ -282,9 +282,11 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--cpu-samples", type=int, default=72)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt-len", type=int, default=PROMPT, help="shorter prompts for profiler runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    globals()["PROMPT"] = args.prompt_len
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -21,35 +21,36 @@
 
 namespace qw {
 
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 8;
+constexpr int kAttnTPW = 8;  // tokens per warp per tile: a tile is 64 tokens
+constexpr int kAttnMaxSplit = 64;
 
-template <typename KT, int DPL> struct KLoad;
-template <> struct KLoad<__nv_bfloat16, 4> {
-    static __device__ __forceinline__ void run(const __nv_bfloat16 *p, float *f) {
-        uint2 u = *reinterpret_cast<const uint2 *>(p);
+// per-lane slice (DPL elements) of one K or V row, kept packed in registers until used
+template <typename KT, int DPL> struct KVec;
+template <> struct KVec<__nv_bfloat16, 4> {
+    using T = uint2;
+    static __device__ __forceinline__ T load(const __nv_bfloat16 *p) { return *reinterpret_cast<const uint2 *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) {
         f[0] = bf16lo(u.x); f[1] = bf16hi(u.x); f[2] = bf16lo(u.y); f[3] = bf16hi(u.y);
     }
 };
-template <> struct KLoad<__nv_bfloat16, 2> {
-    static __device__ __forceinline__ void run(const __nv_bfloat16 *p, float *f) {
-        uint32_t u = *reinterpret_cast<const uint32_t *>(p);
-        f[0] = bf16lo(u); f[1] = bf16hi(u);
-    }
+template <> struct KVec<__nv_bfloat16, 2> {
+    using T = uint32_t;
+    static __device__ __forceinline__ T load(const __nv_bfloat16 *p) { return *reinterpret_cast<const uint32_t *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) { f[0] = bf16lo(u); f[1] = bf16hi(u); }
 };
-template <> struct KLoad<float, 4> {
-    static __device__ __forceinline__ void run(const float *p, float *f) {
-        float4 v = *reinterpret_cast<const float4 *>(p);
-        f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
-    }
+template <> struct KVec<float, 4> {
+    using T = float4;
+    static __device__ __forceinline__ T load(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) { f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w; }
 };
-template <> struct KLoad<float, 2> {
-    static __device__ __forceinline__ void run(const float *p, float *f) {
-        float2 v = *reinterpret_cast<const float2 *>(p);
-        f[0] = v.x; f[1] = v.y;
-    }
+template <> struct KVec<float, 2> {
+    using T = float2;
+    static __device__ __forceinline__ T load(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) { f[0] = u.x; f[1] = u.y; }
 };
 
-__device__ __forceinline__ float block_sum_128(float v, float *scratch) {
+__device__ __forceinline__ float block_sum(float v, float *scratch) {
     v = warp_sum(v);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     __syncthreads();
@@ -61,10 +62,27 @@ __device__ __forceinline__ float block_sum_128(float v, float *scratch) {
     return s;
 }
 
+template <typename KT, int D, int G, int DPL>
+__device__ __forceinline__ void attn_issue(typename KVec<KT, DPL>::T (&kr)[kAttnTPW], typename KVec<KT, DPL>::T (&vr)[kAttnTPW],
+                                           const KT *kc, const KT *vc, const int *ptab, int tbase, int t1, int pos,
+                                           int Hkv, int kvh, int ps, int lg, int warp, int lane) {
+#pragma unroll
+    for (int j = 0; j < kAttnTPW; j++) {
+        const int tt = tbase + warp * kAttnTPW + j;
+        if (tt < t1 && tt != pos) {
+            size_t base = (((size_t)ptab[tt >> lg] * Hkv + kvh) * ps + (tt & (ps - 1))) * D + lane * DPL;
+            kr[j] = KVec<KT, DPL>::load(kc + base);
+            vr[j] = KVec<KT, DPL>::load(vc + base);
+        }
+    }
+}
+
 template <typename KT, int D, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnArgs a) {
     constexpr int DPL = D / 32;
     constexpr int HALF = D / 2;
+    constexpr int TILE = kAttnWarps * kAttnTPW;
+    using KV = KVec<KT, DPL>;
     __shared__ __align__(16) float qs[G][D];
     __shared__ __align__(16) float ks[D];
     __shared__ __align__(16) float vs[D];
@@ -77,8 +95,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = a.H, Hkv = a.Hkv;
+    // positions / slots / page table were written at least two kernels earlier, which have
+    // completed before this grid can start (every kernel triggers its dependents only after its
+    // own wait), so they may be read before the wait below.
     const int slot = a.slots ? a.slots[b] : b;
     const int pos = a.positions[b];
+    // token range of this split: at least 64 tokens per split, so short contexts use few splits
+    const int n = pos + 1;
+    int chunk = (n + a.nsplit - 1) / a.nsplit;
+    chunk = chunk < TILE ? TILE : chunk;
+    const int ns_eff = (n + chunk - 1) / chunk;
+    const int t0 = split * chunk;
+    const int t1 = min(n, t0 + chunk);
+    const int *ptab = a.page_table + (size_t)slot * a.max_pages;
+    const int ps = a.page_size, lg = a.log2_page;
+    KT *kc = reinterpret_cast<KT *>(a.kcache);
+    KT *vc = reinterpret_cast<KT *>(a.vcache);
+
+    typename KV::T kr[kAttnTPW], vr[kAttnTPW], kn[kAttnTPW], vn[kAttnTPW];
+    // the cached K/V rows do not depend on the previous kernel: start loading them now
+    if (t0 < n) attn_issue<KT, D, G, DPL>(kr, vr, kc, vc, ptab, t0, t1, pos, Hkv, kvh, ps, lg, warp, lane);
+    griddep_wait();
+    griddep_launch_dependents();
+
+    if (t0 < n) {
     const float *row = a.qkv + (size_t)b * a.ld_qkv;
     const float *qrow = row + (size_t)kvh * G * D;
     const float *krow = row + (size_t)H * D + (size_t)kvh * D;
@@ -96,10 +136,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
             }
         } else {
             float sq = 0.f, sk = 0.f;
+#pragma unroll 8
             for (int i = tid; i < H * D; i += blockDim.x) sq += row[i] * row[i];
+#pragma unroll 4
             for (int i = tid; i < Hkv * D; i += blockDim.x) sk += row[H * D + i] * row[H * D + i];
-            sq = block_sum_128(sq, scratch);
-            sk = block_sum_128(sk, scratch);
+            sq = block_sum(sq, scratch);
+            sk = block_sum(sk, scratch);
             if (tid == 0) {
                 s_scale[0] = 1.0f / sqrtf(sq / (float)a.q_total + 1e-6f);
                 s_scale[1] = 1.0f / sqrtf(sk / (float)a.kv_total + 1e-6f);
@@ -142,10 +184,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     for (int i = tid; i < D; i += blockDim.x) { ks[i] = Elt<KT>::round(ks[i]); vs[i] = Elt<KT>::round(vs[i]); }
     __syncthreads();
 
-    const int *ptab = a.page_table + (size_t)slot * a.max_pages;
-    const int ps = a.page_size, lg = a.log2_page;
-    KT *kc = reinterpret_cast<KT *>(a.kcache);
-    KT *vc = reinterpret_cast<KT *>(a.vcache);
     if (split == 0) {
         size_t base = (((size_t)ptab[pos >> lg] * Hkv + kvh) * ps + (pos & (ps - 1))) * D;
         for (int i = tid; i < D; i += blockDim.x) {
@@ -154,18 +192,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         }
     }
 
-    // ---------------- main loop over this split's tokens ----------------
-    const int n = pos + 1;
-    int chunk = (n + a.nsplit - 1) / a.nsplit;
-    chunk = chunk < 64 ? 64 : chunk;
-    const int t0 = split * chunk;
-    const int t1 = min(n, t0 + chunk);
-
+    // ---------------- main loop: 64-token tiles, next tile's loads in flight ----------------
     float qreg[G][DPL];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int j = 0; j < DPL; j++) qreg[g][j] = qs[g][lane * DPL + j];
+        for (int j = 0; j < DPL; j++) qreg[g][j] = qs[g][lane * DPL + j] * a.scale;
     float m[G], l[G], o[G][DPL];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -173,44 +205,65 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 #pragma unroll
         for (int j = 0; j < DPL; j++) o[g][j] = 0.f;
     }
+    float kcur[DPL], vcur[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; j++) { kcur[j] = ks[lane * DPL + j]; vcur[j] = vs[lane * DPL + j]; }
 
-    constexpr int U = 2;
-    for (int t = t0 + warp; t < t1; t += kAttnWarps * U) {
-        float kf[U][DPL], vf[U][DPL];
+    for (int tb = t0; tb < t1; tb += TILE) {
+        if (tb + TILE < t1) attn_issue<KT, D, G, DPL>(kn, vn, kc, vc, ptab, tb + TILE, t1, pos, Hkv, kvh, ps, lg, warp, lane);
+        float sc[kAttnTPW][G];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            int tt = t + kAttnWarps * u;
-            if (tt < t1) {
-                if (tt == pos) {
+        for (int j = 0; j < kAttnTPW; j++) {
+            const int tt = tb + warp * kAttnTPW + j;
+            float kf[DPL];
+            if (tt == pos) {
 #pragma unroll
-                    for (int j = 0; j < DPL; j++) { kf[u][j] = ks[lane * DPL + j]; vf[u][j] = vs[lane * DPL + j]; }
-                } else {
-                    size_t base = (((size_t)ptab[tt >> lg] * Hkv + kvh) * ps + (tt & (ps - 1))) * D + lane * DPL;
-                    KLoad<KT, DPL>::run(kc + base, kf[u]);
-                    KLoad<KT, DPL>::run(vc + base, vf[u]);
-                }
+                for (int e = 0; e < DPL; e++) kf[e] = kcur[e];
+            } else {
+                KV::unpack(kr[j], kf);
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float sacc = 0.f;
+#pragma unroll
+                for (int e = 0; e < DPL; e++) sacc = fmaf(qreg[g][e], kf[e], sacc);
+                sc[j][g] = tt < t1 ? warp_sum(sacc) : -INFINITY;
             }
         }
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            int tt = t + kAttnWarps * u;
-            if (tt < t1) {
+        for (int g = 0; g < G; g++) {
+            float mx = m[g];
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    float s = 0.f;
+            for (int j = 0; j < kAttnTPW; j++) mx = fmaxf(mx, sc[j][g]);
+            if (mx == -INFINITY) continue;  // this warp has no tokens in the tile
+            const float alpha = expf(m[g] - mx);
+            l[g] *= alpha;
 #pragma unroll
-                    for (int j = 0; j < DPL; j++) s = fmaf(qreg[g][j], kf[u][j], s);
-                    s = warp_sum(s) * a.scale;
-                    float mn = fmaxf(m[g], s);
-                    float alpha = expf(m[g] - mn);
-                    float p = expf(s - mn);
-                    l[g] = l[g] * alpha + p;
+            for (int e = 0; e < DPL; e++) o[g][e] *= alpha;
+            m[g] = mx;
 #pragma unroll
-                    for (int j = 0; j < DPL; j++) o[g][j] = o[g][j] * alpha + p * vf[u][j];
-                    m[g] = mn;
-                }
+            for (int j = 0; j < kAttnTPW; j++) sc[j][g] = expf(sc[j][g] - mx);
+        }
+#pragma unroll
+        for (int j = 0; j < kAttnTPW; j++) {
+            const int tt = tb + warp * kAttnTPW + j;
+            if (tt >= t1) continue;
+            float vf[DPL];
+            if (tt == pos) {
+#pragma unroll
+                for (int e = 0; e < DPL; e++) vf[e] = vcur[e];
+            } else {
+                KV::unpack(vr[j], vf);
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                l[g] += sc[j][g];
+#pragma unroll
+                for (int e = 0; e < DPL; e++) o[g][e] = fmaf(sc[j][g], vf[e], o[g][e]);
             }
         }
+#pragma unroll
+        for (int j = 0; j < kAttnTPW; j++) { kr[j] = kn[j]; vr[j] = vn[j]; }
     }
 
     // ---------------- merge warps ----------------
@@ -221,8 +274,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         for (int j = 0; j < DPL; j++) wo[warp][g][lane * DPL + j] = o[g][j];
     }
     __syncthreads();
-    const int H_ = H;
-    const int nsplit = a.nsplit;
     for (int i = tid; i < G * D; i += blockDim.x) {
         int g = i / D, j = i % D;
         float M = -INFINITY;
@@ -238,40 +289,53 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
             }
         }
         int h = kvh * G + g;
-        if (nsplit == 1) {
+        if (a.nsplit == 1) {
             a.out[(size_t)b * a.ld_out + (size_t)h * D + j] = O / L;
         } else {
-            size_t pidx = ((size_t)b * H_ + h) * nsplit + split;
+            size_t pidx = ((size_t)b * H + h) * a.nsplit + split;
             a.part_o[pidx * D + j] = O;
             if (j == 0) { a.part_ml[pidx * 2 + 0] = M; a.part_ml[pidx * 2 + 1] = L; }
         }
     }
-    if (nsplit == 1) return;
+    }  // t0 < n
+    if (a.nsplit == 1) return;
 
+    // ---------------- split merge: the last CTA of this (sequence, KV head) ----------------
+    __shared__ float sw[G][kAttnMaxSplit];
     __threadfence();
     __syncthreads();
     if (tid == 0) {
         unsigned t = atomicAdd(a.counters + (size_t)b * Hkv + kvh, 1u);
-        s_last = (t == (unsigned)nsplit - 1);
+        s_last = (t == (unsigned)a.nsplit - 1);
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    const size_t hb = (size_t)b * H + (size_t)kvh * G;  // first head of this group
+    for (int i = tid; i < G * ns_eff; i += blockDim.x) {
+        int g = i / ns_eff, s = i % ns_eff;
+        sw[g][s] = __ldcg(a.part_ml + ((hb + g) * a.nsplit + s) * 2);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int s = 0; s < ns_eff; s++) M = fmaxf(M, sw[tid][s]);
+        float L = 0.f;
+        for (int s = 0; s < ns_eff; s++) {
+            float e = expf(sw[tid][s] - M);
+            L += __ldcg(a.part_ml + ((hb + tid) * a.nsplit + s) * 2 + 1) * e;
+            sw[tid][s] = e;
+        }
+        for (int s = 0; s < ns_eff; s++) sw[tid][s] /= L;
+    }
+    __syncthreads();
     for (int i = tid; i < G * D; i += blockDim.x) {
         int g = i / D, j = i % D;
-        int h = kvh * G + g;
-        size_t p0 = ((size_t)b * H_ + h) * nsplit;
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(a.part_ml + (p0 + s) * 2));
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < nsplit; s++) {
-            float ms = __ldcg(a.part_ml + (p0 + s) * 2);
-            if (ms == -INFINITY) continue;
-            float e = expf(ms - M);
-            L += __ldcg(a.part_ml + (p0 + s) * 2 + 1) * e;
-            O += __ldcg(a.part_o + (p0 + s) * D + j) * e;
-        }
-        a.out[(size_t)b * a.ld_out + (size_t)h * D + j] = O / L;
+        const float *po = a.part_o + (hb + g) * a.nsplit * D + j;
+        float O = 0.f;
+#pragma unroll 4
+        for (int s = 0; s < ns_eff; s++) O += sw[g][s] * __ldcg(po + (size_t)s * D);
+        a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * D + j] = O;
     }
     if (tid == 0) a.counters[(size_t)b * Hkv + kvh] = 0u;
 }

@@ -37,20 +37,6 @@ template <> struct WUnpack<float> {
     }
 };
 
-template <int V>
-__device__ __forceinline__ float dotv(const float *f, const float *x) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < V; i += 4) {
-        float4 xv = *reinterpret_cast<const float4 *>(x + i);
-        s = fmaf(f[i + 0], xv.x, s);
-        s = fmaf(f[i + 1], xv.y, s);
-        s = fmaf(f[i + 2], xv.z, s);
-        s = fmaf(f[i + 3], xv.w, s);
-    }
-    return s;
-}
-
 template <typename WT>
 __device__ __forceinline__ float4 load4(const WT *p);
 template <> __device__ __forceinline__ float4 load4<float>(const float *p) {
@@ -62,17 +48,73 @@ template <> __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bf
 }
 
 constexpr int kGemvThreads = 256;
-constexpr int kGemvUnroll = 4;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvRows = 4;    // rows per CTA tile (SWIGLU: 2 gate + the 2 matching up rows)
+constexpr int kGemvUnroll = 2;  // 16-byte chunks per lane per row per k-step (8 loads in flight per lane)
 
+template <int EPI>
+__device__ __forceinline__ int tile_row(int tile, int r) {
+    if (EPI == EPI_SWIGLU) {
+        int pair = tile * (kGemvRows / 2) + (r % (kGemvRows / 2));
+        int gate = (pair / kGuBlock) * (2 * kGuBlock) + (pair % kGuBlock);
+        return r < kGemvRows / 2 ? gate : gate + kGuBlock;
+    }
+    return tile * kGemvRows + r;
+}
+
+// Issue the weight loads of one pipeline stage (one k-step of one row tile) into registers.
+template <typename WT, int EPI>
+__device__ __forceinline__ void gemv_issue(uint4 (&u)[kGemvRows][kGemvUnroll], const char *Wb, size_t row_bytes,
+                                           int N, int nch, int tile, int kstep, int warp, int lane) {
+    constexpr int NW = kGemvWarps, U = kGemvUnroll, STEP = NW * 32 * U;
+    const int c0 = kstep * STEP + warp * 32 + lane;
+#pragma unroll
+    for (int r = 0; r < kGemvRows; r++) {
+        const int row = tile_row<EPI>(tile, r);
+        const uint4 *w = reinterpret_cast<const uint4 *>(Wb + (size_t)(row < N ? row : 0) * row_bytes);
+#pragma unroll
+        for (int i = 0; i < U; i++) {
+            const int c = c0 + i * NW * 32;
+            u[r][i] = (c < nch && row < N) ? ld_stream(w + c) : make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+// One CTA streams a contiguous range of row tiles; the 8 warps split K of every tile
+// (each warp reads 512 contiguous bytes per row per load), so all warps and all CTAs
+// carry the same number of bytes.  Loads run one stage ahead of the FMAs (register double
+// buffer), the first stage is issued before the programmatic-launch wait so it overlaps the
+// previous kernel's tail, and partial sums meet in shared memory once per tile.
 template <typename WT, int EPI, int NB>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(16) float xs[];  // [NB][K]
-    __shared__ float red[NB][kGemvThreads / 32];
-    __shared__ int redi[NB][kGemvThreads / 32];
+    __shared__ float red[2][kGemvWarps][kGemvRows * NB];
+    __shared__ float am_v[kGemvRows * NB];
+    __shared__ int am_i[kGemvRows * NB];
     __shared__ int s_is_last;
     const int K = a.K;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int NW = kGemvThreads / 32;
+    constexpr int NW = kGemvWarps;
+    constexpr int R = kGemvRows;
+    constexpr int U = kGemvUnroll;
+    constexpr int V = WUnpack<WT>::V;
+    constexpr int STEP = NW * 32 * U;  // 16-byte chunks per k-step of the whole CTA
+
+    const int nch = K / V;
+    const int N = a.N;
+    const int ntiles = (EPI == EPI_SWIGLU) ? (N / 2) / (R / 2) : (N + R - 1) / R;
+    const int t_begin = (int)(((long long)ntiles * blockIdx.x) / gridDim.x);
+    const int t_end = (int)(((long long)ntiles * (blockIdx.x + 1)) / gridDim.x);
+    const size_t row_bytes = (size_t)K * sizeof(WT);
+    const char *Wb = reinterpret_cast<const char *>(a.W);
+    const int ksteps = (nch + STEP - 1) / STEP;
+    const int nstage = (t_end - t_begin) * ksteps;
+
+    // weights do not depend on the previous kernel: start streaming them before the wait
+    uint4 ucur[R][U], unext[R][U];
+    if (nstage > 0) gemv_issue<WT, EPI>(ucur, Wb, row_bytes, N, nch, t_begin, 0, warp, lane);
+    griddep_wait();
+    griddep_launch_dependents();
 
     // ---------------- prologue: activation row(s) -> shared memory ----------------
     float ss[NB];
@@ -95,16 +137,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float s = warp_sum(ss[b]);
-            if (lane == 0) red[b][warp] = s;
+            if (lane == 0) red[0][warp][b] = s;
         }
         __syncthreads();
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float s = 0.f;
 #pragma unroll
-            for (int w = 0; w < NW; w++) s += red[b][w];
+            for (int w = 0; w < NW; w++) s += red[0][w][b];
             ss[b] = 1.0f / sqrtf(s / (float)K + a.eps);
         }
+        __syncthreads();
 #pragma unroll
         for (int b = 0; b < NB; b++)
             for (int k = tid * 4; k < K; k += kGemvThreads * 4) {
@@ -117,106 +160,101 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     }
     __syncthreads();
 
-    // ---------------- main: two rows per warp, contiguous task range per CTA ----------------
-    constexpr int V = WUnpack<WT>::V;
-    const int nch = K / V;
-    const int ntask = (EPI == EPI_SWIGLU) ? a.N / 2 : (a.N + 1) / 2;
-    const int t_begin = (int)(((long long)ntask * blockIdx.x) / gridDim.x);
-    const int t_end = (int)(((long long)ntask * (blockIdx.x + 1)) / gridDim.x);
-    const size_t row_bytes = (size_t)K * sizeof(WT);
-    const char *Wb = reinterpret_cast<const char *>(a.W);
-
-    float bestv[NB];
-    int besti[NB];
+    // ---------------- main: pipelined stages ----------------
+    float bestv = -FLT_MAX;  // ARGMAX: per epilogue thread (r, b)
+    int besti = INT_MAX;
+    float acc[R][NB];
 #pragma unroll
-    for (int b = 0; b < NB; b++) { bestv[b] = -FLT_MAX; besti[b] = INT_MAX; }
-
-    for (int task = t_begin + warp; task < t_end; task += NW) {
-        int r0, r1;
-        bool v1;
-        if (EPI == EPI_SWIGLU) {
-            r0 = (task / kGuBlock) * (2 * kGuBlock) + (task % kGuBlock);
-            r1 = r0 + kGuBlock;
-            v1 = true;
-        } else {
-            r0 = 2 * task;
-            v1 = (r0 + 1) < a.N;
-            r1 = v1 ? r0 + 1 : r0;
-        }
-        const uint4 *w0 = reinterpret_cast<const uint4 *>(Wb + (size_t)r0 * row_bytes);
-        const uint4 *w1 = reinterpret_cast<const uint4 *>(Wb + (size_t)r1 * row_bytes);
-        float acc0[NB], acc1[NB];
+    for (int r = 0; r < R; r++)
 #pragma unroll
-        for (int b = 0; b < NB; b++) { acc0[b] = 0.f; acc1[b] = 0.f; }
-
-        for (int c0 = lane; c0 < nch; c0 += 32 * kGemvUnroll) {
-            uint4 u0[kGemvUnroll], u1[kGemvUnroll];
+        for (int b = 0; b < NB; b++) acc[r][b] = 0.f;
+    int buf = 0;
+    for (int st = 0; st < nstage; st++) {
+        const int tile = t_begin + st / ksteps, kstep = st % ksteps;
+        if (st + 1 < nstage)
+            gemv_issue<WT, EPI>(unext, Wb, row_bytes, N, nch, t_begin + (st + 1) / ksteps, (st + 1) % ksteps, warp,
+                                lane);
+        const int c0 = kstep * STEP + warp * 32 + lane;
 #pragma unroll
-            for (int i = 0; i < kGemvUnroll; i++) {
-                int c = c0 + 32 * i;
-                if (c < nch) { u0[i] = ld_stream(w0 + c); u1[i] = ld_stream(w1 + c); }
-            }
+        for (int i = 0; i < U; i++) {
+            const int c = c0 + i * NW * 32;
+            if (c < nch) {
 #pragma unroll
-            for (int i = 0; i < kGemvUnroll; i++) {
-                int c = c0 + 32 * i;
-                if (c < nch) {
-                    float f0[V], f1[V];
-                    WUnpack<WT>::run(u0[i], f0);
-                    WUnpack<WT>::run(u1[i], f1);
+                for (int b = 0; b < NB; b++) {
+                    float xv[V];
 #pragma unroll
-                    for (int b = 0; b < NB; b++) {
-                        const float *xv = xs + b * K + c * V;
-                        acc0[b] += dotv<V>(f0, xv);
-                        acc1[b] += dotv<V>(f1, xv);
+                    for (int j = 0; j < V; j += 4) {
+                        float4 t4 = *reinterpret_cast<const float4 *>(xs + b * K + c * V + j);
+                        xv[j] = t4.x; xv[j + 1] = t4.y; xv[j + 2] = t4.z; xv[j + 3] = t4.w;
+                    }
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        float f[V];
+                        WUnpack<WT>::run(ucur[r][i], f);
+                        float sacc = acc[r][b];
+#pragma unroll
+                        for (int j = 0; j < V; j++) sacc = fmaf(f[j], xv[j], sacc);
+                        acc[r][b] = sacc;
                     }
                 }
             }
         }
 #pragma unroll
-        for (int b = 0; b < NB; b++) { acc0[b] = warp_sum(acc0[b]); acc1[b] = warp_sum(acc1[b]); }
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int i = 0; i < U; i++) ucur[r][i] = unext[r][i];
+        if (kstep != ksteps - 1) continue;
 
-        if (lane == 0) {
+        // ---- tile complete: reduce over warps, epilogue ----
+#pragma unroll
+        for (int r = 0; r < R; r++)
 #pragma unroll
             for (int b = 0; b < NB; b++) {
-                if (EPI == EPI_STORE) {
-                    float* o = a.out + (size_t)b * a.ld_out;
-                    o[r0] = acc0[b] + (a.bias ? a.bias[r0] : 0.f);
-                    if (v1) o[r1] = acc1[b] + (a.bias ? a.bias[r1] : 0.f);
-                } else if (EPI == EPI_RESID) {
-                    float* o = a.out + (size_t)b * a.ld_out;
-                    const float *rs = a.resid ? a.resid + (size_t)b * a.ld_resid : nullptr;
-                    o[r0] = (rs ? rs[r0] : 0.f) + acc0[b];
-                    if (v1) o[r1] = (rs ? rs[r1] : 0.f) + acc1[b];
-                } else if (EPI == EPI_SWIGLU) {
-                    float g = acc0[b], u = acc1[b];
+                float v = warp_sum(acc[r][b]);
+                acc[r][b] = 0.f;
+                if (lane == 0) red[buf][warp][r * NB + b] = v;
+            }
+        __syncthreads();
+        if (tid < R * NB) {
+            const int r = tid / NB, b = tid % NB;
+            float y = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) y += red[buf][w][tid];
+            const int row = tile_row<EPI>(tile, r);
+            if (EPI == EPI_STORE) {
+                if (row < N) a.out[(size_t)b * a.ld_out + row] = y + (a.bias ? a.bias[row] : 0.f);
+            } else if (EPI == EPI_RESID) {
+                if (row < N)
+                    a.out[(size_t)b * a.ld_out + row] = (a.resid ? a.resid[(size_t)b * a.ld_resid + row] : 0.f) + y;
+            } else if (EPI == EPI_SWIGLU) {
+                if (r < R / 2) {
+                    float g = y;
+                    float u = 0.f;
+#pragma unroll
+                    for (int w = 0; w < NW; w++) u += red[buf][w][(r + R / 2) * NB + b];
                     float sg = 1.0f / (1.0f + expf(-g));
-                    a.out[(size_t)b * a.ld_out + task] = u * (g * sg);
-                } else {  // EPI_ARGMAX
-                    if (a.out) {
-                        float* o = a.out + (size_t)b * a.ld_out;
-                        o[r0] = acc0[b];
-                        if (v1) o[r1] = acc1[b];
-                    }
-                    if (acc0[b] > bestv[b]) { bestv[b] = acc0[b]; besti[b] = r0; }
-                    if (v1 && acc1[b] > bestv[b]) { bestv[b] = acc1[b]; besti[b] = r1; }
+                    int pair = tile * (R / 2) + r;
+                    a.out[(size_t)b * a.ld_out + pair] = u * (g * sg);
+                }
+            } else {  // EPI_ARGMAX: rows increase within a thread, so strict > keeps the first max
+                if (row < N) {
+                    if (a.out) a.out[(size_t)b * a.ld_out + row] = y;
+                    if (y > bestv) { bestv = y; besti = row; }
                 }
             }
         }
+        buf ^= 1;
     }
 
     if (EPI == EPI_ARGMAX) {
-        // CTA reduction (ties -> smaller index), then the last CTA reduces over the grid.
-        if (lane == 0) {
-#pragma unroll
-            for (int b = 0; b < NB; b++) { red[b][warp] = bestv[b]; redi[b][warp] = besti[b]; }
-        }
+        if (tid < R * NB) { am_v[tid] = bestv; am_i[tid] = besti; }
         __syncthreads();
         if (tid < NB) {
             float bv = -FLT_MAX;
             int bi = INT_MAX;
-            for (int w = 0; w < NW; w++) {
-                float v = red[tid][w];
-                int i = redi[tid][w];
+            for (int r = 0; r < R; r++) {
+                float v = am_v[r * NB + tid];
+                int i = am_i[r * NB + tid];
                 if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
             }
             a.part_val[blockIdx.x * NB + tid] = bv;
@@ -272,8 +310,18 @@ static int prepare_cached(const void *fn, size_t smem, cudaError_t *err) {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find({fn, smem});
     if (it != cache.end()) return it->second;
-    *err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (*err != cudaSuccess) return 0;
+    // one opt-in to the largest size per kernel: a smaller later setting would invalidate
+    // launches of larger, already-cached sizes
+    static std::map<const void *, bool> opted;
+    if (!opted[fn]) {
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        int stat_smem = 4096;  // static shared memory margin
+        *err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - stat_smem);
+        if (*err != cudaSuccess) return 0;
+        opted[fn] = true;
+    }
     int occ = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kGemvThreads, smem) != cudaSuccess || occ < 1) occ = 1;
     cache[{fn, smem}] = occ;
@@ -287,12 +335,11 @@ static cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t st) {
     cudaError_t e = cudaSuccess;
     int occ = prepare_cached((const void *)kfn, smem, &e);
     if (e != cudaSuccess) return e;
-    int ntask = (EPI == EPI_SWIGLU) ? a.N / 2 : (a.N + 1) / 2;
-    int want = (ntask + (kGemvThreads / 32) - 1) / (kGemvThreads / 32);
+    // persistent grid: every SM holds `occ` CTAs for the whole launch
+    int ntiles = (EPI == EPI_SWIGLU) ? (a.N / 2) / (kGemvRows / 2) : (a.N + kGemvRows - 1) / kGemvRows;
     int cap = num_sms * occ;
-    int grid = want < cap ? (want > 0 ? want : 1) : cap;
-    kfn<<<grid, kGemvThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    int grid = ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap;
+    return launch_pdl(kfn, dim3(grid), dim3(kGemvThreads), smem, st, a);
 }
 
 template <typename WT, int EPI>

@@ -35,6 +35,7 @@ cudaError_t freq_launch(float2 *freq, int seq_len, int head_dim, double theta, c
 cudaError_t argmax_merge_launch(const float *vals, const int *idxs, int tp, int B, int *argmax_out, int *next_tokens,
                                 int *positions, int advance, int *hist, int hist_ld, cudaStream_t st);
 cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, float *out, cudaStream_t st);
+cudaError_t hold_launch(unsigned long long ns, cudaStream_t st);
 cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cudaStream_t st);
 
 cudaError_t gemv_launch(const GemvArgs &a, int epi, bool bf16, int num_sms, cudaStream_t st);

@@ -132,4 +132,20 @@ cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cud
     return cudaGetLastError();
 }
 
+// Bounded busy-wait of `ns` nanoseconds on the device (globaltimer), used to let the host
+// run ahead of the GPU before a profiled sequence of launches.  Ends by itself.
+__global__ void hold_kernel(unsigned long long ns) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (int i = 0; i < (1 << 24); i++) {
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 >= ns) break;
+        __nanosleep(1000);
+    }
+}
+cudaError_t hold_launch(unsigned long long ns, cudaStream_t st) {
+    hold_kernel<<<1, 32, 0, st>>>(ns);
+    return cudaGetLastError();
+}
+
 }  // namespace qw

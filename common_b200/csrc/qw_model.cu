@@ -858,6 +858,8 @@ qw_status qw_profile_decode(qw_model *m, int32_t batch, float *ms_out, int32_t *
     }
     m->prof_kinds.assign(cap, 0);
     m->prof_n = 0;
+    // keep the GPU busy while the host enqueues the step, so event pairs bracket device time only
+    CK(hold_launch(20ull * 1000 * 1000, m->st));
     m->prof_on = true;
     // positions / tokens / slots are the model's own device buffers (current contents)
     qw_status s = device_step(m, m->d_tokens, nullptr, m->d_slots, m->d_pos, batch, nullptr, m->d_argmax, 0, nullptr, 0);

@@ -224,3 +224,12 @@ def test_qwen3_api_mirror():
     emb = sd["model.embed_tokens.weight"]
     lg = q.getCompiledModel().forward(emb[9][None])
     assert rel_l2(lg[0], o.forward_token(9, 0)) < FP32_TOL
+
+
+def test_bf16_8b_layer_geometry():
+    """One layer at the Qwen3-8B geometry (K = 4096 and 12288 GEMVs, 32/8 heads, d 128)."""
+    c = cfg_dict(dim=4096, hidden_dim=12288, layers=1, heads=32, kv_heads=8, head_dim=128, vocab=8192, seq_len=80)
+    sd = state_dict(c, seed=19, std=0.02)
+    toks = np.random.default_rng(20).integers(0, c["vocab"], 70)
+    errs = run_both(c, sd, toks, precision="bf16", bf16_oracle=True)
+    assert errs.max() < BF16_TOL, errs.max()
