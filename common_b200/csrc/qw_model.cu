@@ -17,6 +17,7 @@
 #include "../../include/qwen3_b200.h"
 #include "qw_kernels.h"
 #include "qw_prefill.h"
+#include "qw_ops.h"
 
 using namespace qw;
 
@@ -898,7 +899,7 @@ void *qw_stream(qw_model *m) { return m ? (void *)m->st : nullptr; }
 
 int32_t qw_last_launch_count(const qw_model *m) { return m ? m->launches : 0; }
 
-const char *qw_last_error(const qw_model *m) { return m ? m->err.c_str() : "null model"; }
+const char *qw_last_error(const qw_model *m) { return m ? m->err.c_str() : qw::op_last_error(); }
 
 void qw_destroy(qw_model *m) {
     if (!m) return;

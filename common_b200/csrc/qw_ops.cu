@@ -1,0 +1,93 @@
+// qw_ops.cu -- op-level entry points: single fused kernels over caller-provided device buffers.
+//
+// The reference enters its generated kernels one operation at a time through JNI
+// (NativeInstructionSet.java:39-121); these entry points expose individual fused kernels of
+// this library the same way, for hosts that keep their own device buffers.
+#include <cuda_runtime.h>
+#include <mutex>
+#include <string>
+
+#include "../../include/qwen3_b200.h"
+#include "qw_kernels.h"
+#include "qw_ops.h"
+
+namespace qw {
+
+static thread_local std::string g_op_error;
+
+qw_status op_fail(qw_status s, const std::string &msg) {
+    g_op_error = msg;
+    return s;
+}
+
+const char *op_last_error() { return g_op_error.c_str(); }
+
+qw_status op_lm_head_check(const void *w, int32_t w_dtype, int32_t vocab, int32_t dim, const float *x,
+                           const float *norm_w, int32_t batch, const int32_t *argmax_out) {
+    if (!w || !x || !norm_w || !argmax_out) return op_fail(QW_ERR_ARG, "null device pointer");
+    if (w_dtype != QW_DTYPE_F32 && w_dtype != QW_DTYPE_BF16) return op_fail(QW_ERR_UNSUPPORTED, "weight dtype");
+    if (vocab < 1 || dim < 8 || dim % 8) return op_fail(QW_ERR_SHAPE, "vocab >= 1 and dim a positive multiple of 8");
+    if (batch < 1 || batch > kGemvMaxB) return op_fail(QW_ERR_SHAPE, "batch must be in [1, 4]");
+    return QW_OK;
+}
+
+GemvArgs op_lm_head_args(const void *w, int32_t vocab, int32_t dim, const float *x, const float *norm_w, double eps,
+                         int32_t batch, float *logits_out, int32_t *argmax_out, float *part_val, int *part_idx,
+                         unsigned *counter) {
+    GemvArgs g{};
+    g.W = w; g.N = vocab; g.K = dim; g.B = batch;
+    g.xin = x; g.ld_in = dim;
+    g.norm_w = norm_w; g.eps = (float)eps;
+    g.out = logits_out; g.ld_out = vocab;
+    g.part_val = part_val; g.part_idx = part_idx; g.counter = counter;
+    g.argmax_out = argmax_out;
+    return g;
+}
+
+}  // namespace qw
+
+using namespace qw;
+
+namespace {
+// per-device scratch of qw_op_lm_head_argmax, allocated on first use and kept
+struct OpScratch {
+    float *val = nullptr;
+    int *idx = nullptr;
+    unsigned *counter = nullptr;
+};
+std::mutex g_scratch_mu;
+OpScratch g_scratch[64];
+}  // namespace
+
+extern "C" qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_t vocab, int32_t dim, const float *x,
+                                          const float *norm_w, double eps, int32_t batch, float *logits_out,
+                                          int32_t *argmax_out, void *stream) {
+    qw_status s = op_lm_head_check(w, w_dtype, vocab, dim, x, norm_w, batch, argmax_out);
+    if (s) return s;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return op_fail(QW_ERR_CUDA, "no current device");
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return op_fail(QW_ERR_CUDA, "device query failed");
+    cudaStream_t st = (cudaStream_t)stream;
+    OpScratch *sc;
+    {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        sc = &g_scratch[dev];
+        if (!sc->val) {
+            size_t n = (size_t)sms * kGemvMaxCtasPerSm * kGemvMaxB;
+            if (cudaMalloc(&sc->val, n * sizeof(float)) != cudaSuccess ||
+                cudaMalloc(&sc->idx, n * sizeof(int)) != cudaSuccess ||
+                cudaMalloc(&sc->counter, sizeof(unsigned)) != cudaSuccess ||
+                cudaMemset(sc->counter, 0, sizeof(unsigned)) != cudaSuccess) {
+                cudaFree(sc->val); cudaFree(sc->idx); cudaFree(sc->counter);
+                *sc = OpScratch{};
+                return op_fail(QW_ERR_OOM, "scratch allocation failed");
+            }
+        }
+    }
+    GemvArgs g = op_lm_head_args(w, vocab, dim, x, norm_w, eps, batch, logits_out, argmax_out, sc->val, sc->idx,
+                                 sc->counter);
+    cudaError_t e = gemv_launch(g, EPI_ARGMAX, w_dtype == QW_DTYPE_BF16, sms, st);
+    if (e != cudaSuccess) return op_fail(QW_ERR_CUDA, std::string("lm_head/argmax launch: ") + cudaGetErrorString(e));
+    return QW_OK;
+}

@@ -196,7 +196,24 @@ void *qw_stream(qw_model *m);
 /* Number of kernel launches the last decode step / prefill enqueued. */
 int32_t qw_last_launch_count(const qw_model *m);
 
-/* Human-readable description of the last error on this model (never NULL). */
+/* ---------------------------------------------------------------------------------------
+ * Op-level entry points: one fused kernel over caller-provided DEVICE buffers, enqueued on
+ * `stream` (a cudaStream_t, NULL = legacy default stream) of the current device.
+ * -------------------------------------------------------------------------------------- */
+
+/* Greedy sampling tail of the step: logits = W . rmsnorm(x; norm_w, eps) for `batch` (1..4)
+ * hidden rows x (batch, dim) fp32, W (vocab, dim) in w_dtype (F32 or BF16); writes the
+ * logits (batch, vocab) fp32 when logits_out is not NULL and the first index of the maximum
+ * per row to argmax_out (batch) int32.  Stands in for rmsnorm(final) + dense(wcls) +
+ * indexOfMax (Qwen3.java:402-405, AggregationFeatures.java:111-121,
+ * AutoregressiveModel.java:412-420).  Its cross-CTA scratch is allocated with cudaMalloc on
+ * the first call per device and kept for the life of the process. */
+qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_t vocab, int32_t dim, const float *x,
+                               const float *norm_w, double eps, int32_t batch, float *logits_out,
+                               int32_t *argmax_out, void *stream);
+
+/* Human-readable description of the last error on this model (never NULL).  With m == NULL:
+ * the last error of an op-level entry point on this thread. */
 const char *qw_last_error(const qw_model *m);
 
 void qw_destroy(qw_model *m);
