@@ -212,6 +212,21 @@ qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_t vocab, in
                                const float *norm_w, double eps, int32_t batch, float *logits_out,
                                int32_t *argmax_out, void *stream);
 
+/* qw_op_lm_head_argmax with no allocation anywhere: same arguments, results and errors,
+ * but its cross-CTA scratch is a fixed 64 KiB array compiled into the library (held on every
+ * GPU that loads it until the process exits) instead of memory from cudaMalloc.  For hosts
+ * that cannot allocate device memory themselves or through this library -- a JVM that only
+ * passes pointers into its own pool, a process whose caching allocator must own every byte.
+ * No counterpart in the reference (its generated kernels never need scratch).
+ * Limit: sm_count * 8 * batch <= 8192 (every current GPU at batch <= 4); beyond it the call
+ * returns QW_ERR_SHAPE.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any stream
+ * capture.  All calls share the one array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller. */
+qw_status qw_op_lm_head_argmax_static(const void *w, int32_t w_dtype, int32_t vocab, int32_t dim, const float *x,
+                                      const float *norm_w, double eps, int32_t batch, float *logits_out,
+                                      int32_t *argmax_out, void *stream);
+
 /* Human-readable description of the last error on this model (never NULL).  With m == NULL:
  * the last error of an op-level entry point on this thread. */
 const char *qw_last_error(const qw_model *m);
