@@ -1,0 +1,435 @@
+// qw_gemm.cu -- the projections of prefill and batched decode on the 5th-generation tensor
+// cores: tcgen05.mma with the accumulator in tensor memory (TMEM), operands staged in
+// 128-byte-swizzled shared memory by TMA (cp.async.bulk.tensor, no multicast).
+//
+// Stands in for the reference's dense layer (LayerFeatures.dense, domain/graph/src/main/java/
+// org/almostrealism/layers/LayerFeatures.java:785-830: y = W x with W (out, in) row-major)
+// applied to many rows at once, with the neighbouring element-wise work fused into the
+// epilogue: bias (Qwen2.5 layout), the residual accumulation of SequentialBlock.accum
+// (SequentialBlock.java:413-429) and the SwiGLU product of FeedForwardFeatures.java:147-156.
+//
+// Layout of one CTA (persistent, one per SM, 192 threads):
+//   warp 0      TMA producer: for every k-block, one 128 x 64 tile of W and one BN x 64 tile
+//               of X into a ring of S shared-memory stages (full / empty mbarriers);
+//   warp 1      allocates 2*BN TMEM columns; one lane issues 4 tcgen05.mma (M=128, N=BN,
+//               K=16) per stage and commits the stage back to the producer, then commits the
+//               finished accumulator to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output features), fused
+//               epilogue, coalesced stores (consecutive features across a warp).
+// Two accumulators in TMEM let the epilogue of tile i overlap the MMAs of tile i+1.
+// Tiles are visited in groups of 8 token tiles so that the CTAs running at the same time share
+// their W and X tiles in L2.
+//
+// Every mbarrier wait is bounded (kTcWaitNs); on expiry the CTA records TC_DEVERR_TIMEOUT,
+// lets its issued copies and MMAs land, frees its TMEM and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <mutex>
+
+#include "qw_internal.cuh"
+#include "qw_tc.h"
+
+namespace qw {
+
+namespace {
+
+constexpr int kTcThreads = 192;
+constexpr int kBM = 128, kBK = 64;
+constexpr int kGroupT = 8;
+constexpr unsigned long long kTcWaitNs = 2000ull * 1000ull * 1000ull;  // 2 s
+constexpr int kTcSmemBudget = 196 * 1024;
+
+__host__ __device__ constexpr int tc_stage_bytes(int bn) { return (kBM + bn) * kBK * 2; }
+__host__ __device__ constexpr int tc_stages(int bn) {
+    return kTcSmemBudget / tc_stage_bytes(bn) > 8 ? 8 : kTcSmemBudget / tc_stage_bytes(bn);
+}
+__host__ __device__ constexpr int tc_smem_bytes(int bn) { return tc_stages(bn) * tc_stage_bytes(bn) + 1024; }
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t gtime_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+
+// Bounded wait: false when the CTA is aborting or the limit expired (which starts the abort).
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+    const uint32_t addr = smem_u32(b);
+    if (mbar_try(addr, parity)) return true;
+    const uint64_t t0 = gtime_ns();
+    for (;;) {
+        if (mbar_try(addr, parity)) return true;
+        if (*abort_flag) return false;
+        if (gtime_ns() - t0 > kTcWaitNs) {
+            *abort_flag = 1;
+            if (err) atomicExch(err, TC_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major tile, rows of 128 bytes with the 128-byte swizzle,
+// 8-row core groups 1024 bytes apart (stride byte offset), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1 << 16;            // leading byte offset (unused by swizzled K-major layouts)
+    d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset
+    d |= (uint64_t)1 << 46;            // version
+    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B (both K-major), fp32 D, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t tc_idesc(int bn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct TileCoord {
+    int f0, t0, kb0, kb1, ks;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int tile, int nf, int nt, int nks, int nkb) {
+    TileCoord c;
+    c.ks = tile % nks;
+    const int j = tile / nks;
+    const int per_group = nf * kGroupT;
+    const int g = j / per_group, r = j % per_group;
+    const int t_in = min(kGroupT, nt - g * kGroupT);
+    c.t0 = (g * kGroupT + r % t_in);
+    c.f0 = (r / t_in) * kBM;
+    c.kb0 = (int)(((long long)nkb * c.ks) / nks);
+    c.kb1 = (int)(((long long)nkb * (c.ks + 1)) / nks);
+    return c;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
+    constexpr int S = tc_stages(BN);
+    constexpr int A_BYTES = kBM * kBK * 2, B_BYTES = BN * kBK * 2;
+    constexpr uint32_t TMEM_COLS = 2 * BN;
+    constexpr uint32_t IDESC = tc_idesc(BN);
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S], tfull_bar[2], tempty_bar[2], done_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * A_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int *abort_flag = &abort_sh;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tfull_bar[i], 1);
+            mbar_init(&tempty_bar[i], 4);
+        }
+        mbar_init(&done_bar, 1);
+        abort_sh = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmW) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmX) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+
+    const int nf = (a.M + kBM - 1) / kBM, nt = (a.T + BN - 1) / BN, nks = a.ksplit;
+    const int nkb = (a.K + kBK - 1) / kBK;
+    const int total = nf * nt * nks;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int s = 0;
+            uint32_t ph = 0, issued = 0, last_ph = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const TileCoord c = tile_coord(tile, nf, nt, nks, nkb);
+                for (int kb = c.kb0; kb < c.kb1; kb++) {
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, a.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full_bar[s], A_BYTES + B_BYTES);
+                    tma_load_2d(sA + s * A_BYTES, &tmW, &full_bar[s], kb * kBK, c.f0);
+                    tma_load_2d(sB + s * B_BYTES, &tmX, &full_bar[s], kb * kBK, c.t0 * BN);
+                    issued |= 1u << s;
+                    last_ph = (last_ph & ~(1u << s)) | (ph << s);
+                    if (++s == S) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // let every issued copy land before the CTA's shared memory goes away
+                for (int i = 0; i < S; i++)
+                    if (issued >> i & 1u) {
+                        const uint32_t addr = smem_u32(&full_bar[i]);
+                        const uint64_t t0 = gtime_ns();
+                        while (!mbar_try(addr, (last_ph >> i) & 1u) && gtime_ns() - t0 < kTcWaitNs) {
+                        }
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            int s = 0, it = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, it++) {
+                const TileCoord c = tile_coord(tile, nf, nt, nks, nkb);
+                const int acc = it & 1;
+                const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+                if (!mbar_wait(&tempty_bar[acc], aph ^ 1u, abort_flag, a.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * BN);
+                for (int kb = c.kb0; kb < c.kb1; kb++) {
+                    if (!mbar_wait(&full_bar[s], ph, abort_flag, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
+                    const uint64_t bd = sw128_desc(smem_u32(sB + s * B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        tc_mma(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb > c.kb0 || k > 0) ? 1u : 0u);
+                    tc_commit(&empty_bar[s]);
+                    if (++s == S) { s = 0; ph ^= 1u; }
+                }
+                if (ok) tc_commit(&tfull_bar[acc]);
+            }
+            // all MMAs of this CTA complete before the TMEM is freed
+            tc_commit(&done_bar);
+            const uint32_t addr = smem_u32(&done_bar);
+            const uint64_t t0 = gtime_ns();
+            while (!mbar_try(addr, 0) && gtime_ns() - t0 < kTcWaitNs) {
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int it = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
+            const TileCoord c = tile_coord(tile, nf, nt, nks, nkb);
+            const int acc = it & 1;
+            const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+            if (!mbar_wait(&tfull_bar[acc], aph, abort_flag, a.err)) break;
+            tc_fence_after();
+            const int f = c.f0 + q * 32 + lane;
+            const int tbase = c.t0 * BN;
+            const int ncols = min(BN, a.T - tbase);
+            for (int cc = 0; cc < ncols; cc += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + cc), r);
+                const int nj = min(32, ncols - cc);
+                if (EPI == TC_SWIGLU) {
+                    __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(a.out);
+                    const int pair = ((c.f0 + q * 32) >> 1) + lane;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float g = __uint_as_float(r[j]);
+                        const float u = __shfl_down_sync(0xffffffffu, g, 16);
+                        if (lane < 16 && j < nj && c.f0 + q * 32 < a.M) {
+                            const float sg = 1.0f / (1.0f + expf(-g));
+                            o[(size_t)(tbase + cc + j) * a.ld_out + pair] = __float2bfloat16_rn(u * (g * sg));
+                        }
+                    }
+                } else if (f < a.M) {
+                    float *o = reinterpret_cast<float *>(a.out);
+                    const float bias = (a.bias && c.ks == 0) ? a.bias[f] : 0.f;
+                    if (nks > 1) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < nj) atomicAdd(o + (size_t)(tbase + cc + j) * a.ld_out + f, __uint_as_float(r[j]) + bias);
+                    } else if (EPI == TC_RESID) {
+                        // all residual loads first (out may alias resid), then the stores
+                        float rv[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            rv[j] = j < nj ? a.resid[(size_t)(tbase + cc + j) * a.ld_resid + f] : 0.f;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < nj) o[(size_t)(tbase + cc + j) * a.ld_out + f] = rv[j] + __uint_as_float(r[j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < nj) o[(size_t)(tbase + cc + j) * a.ld_out + f] = __uint_as_float(r[j]) + bias;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// bf16 (rows, cols) row-major, box of box_rows x 64 columns, 128-byte swizzle, zero fill
+cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols % 8)) return cudaErrorMisalignedAddress;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_bn(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a, int num_sms, cudaStream_t st) {
+    auto kfn = tc_gemm_kernel<BN, EPI>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute((const void *)kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes(BN));
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    const int nf = (a.M + kBM - 1) / kBM, nt = (a.T + BN - 1) / BN;
+    const int total = nf * nt * a.ksplit;
+    const int grid = total < num_sms ? total : num_sms;
+    kfn<<<grid, kTcThreads, tc_smem_bytes(BN), st>>>(mw, mx, a);
+    return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t launch_epi(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a, int bn, int num_sms,
+                       cudaStream_t st) {
+    switch (bn) {
+        case 64: return launch_bn<64, EPI>(mw, mx, a, num_sms, st);
+        case 128: return launch_bn<128, EPI>(mw, mx, a, num_sms, st);
+        case 256: return launch_bn<256, EPI>(mw, mx, a, num_sms, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int tc_pick_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
+
+int tc_pick_ksplit(int M, int T, int K, int bn, int num_sms) {
+    const int tiles = ((M + kBM - 1) / kBM) * ((T + bn - 1) / bn);
+    const int nkb = (K + kBK - 1) / kBK;
+    if (tiles >= num_sms / 2) return 1;
+    int ks = (num_sms + tiles - 1) / tiles;
+    ks = ks > nkb / 2 ? nkb / 2 : ks;  // at least two k-blocks per split
+    return ks < 1 ? 1 : ks;
+}
+
+cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int epi, int bn, int num_sms,
+                           cudaStream_t st) {
+    if (a.M < 1 || a.T < 1 || a.K < 8 || a.K % 8 || a.ksplit < 1) return cudaErrorInvalidValue;
+    if (a.ksplit > (a.K + kBK - 1) / kBK) return cudaErrorInvalidValue;
+    if (epi == TC_SWIGLU && (a.ksplit != 1 || a.M % 32)) return cudaErrorInvalidValue;
+    if (epi == TC_RESID && a.ksplit > 1 && a.out != (const void *)a.resid) return cudaErrorInvalidValue;
+    if (bn == 0) bn = tc_pick_bn(a.T);
+    CUtensorMap mw, mx;
+    cudaError_t e = make_map(&mw, W, a.M, a.K, kBM);
+    if (e != cudaSuccess) return e;
+    e = make_map(&mx, X, a.T, a.K, bn);
+    if (e != cudaSuccess) return e;
+    switch (epi) {
+        case TC_STORE: return launch_epi<TC_STORE>(mw, mx, a, bn, num_sms, st);
+        case TC_RESID: return launch_epi<TC_RESID>(mw, mx, a, bn, num_sms, st);
+        case TC_SWIGLU: return launch_epi<TC_SWIGLU>(mw, mx, a, bn, num_sms, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace qw

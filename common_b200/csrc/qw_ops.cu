@@ -10,6 +10,7 @@
 #include "../../include/qwen3_b200.h"
 #include "qw_kernels.h"
 #include "qw_ops.h"
+#include "qw_tc.h"
 
 namespace qw {
 
@@ -89,5 +90,25 @@ extern "C" qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_
                                  sc->counter);
     cudaError_t e = gemv_launch(g, EPI_ARGMAX, w_dtype == QW_DTYPE_BF16, sms, st);
     if (e != cudaSuccess) return op_fail(QW_ERR_CUDA, std::string("lm_head/argmax launch: ") + cudaGetErrorString(e));
+    return QW_OK;
+}
+
+extern "C" qw_status qw_op_linear(const void *w, int32_t n_out, int32_t k, const void *x, int32_t t, int32_t epi,
+                                  const float *bias, const float *resid, void *out, void *stream) {
+    if (!w || !x || !out) return op_fail(QW_ERR_ARG, "null device pointer");
+    if (epi < QW_LINEAR_STORE || epi > QW_LINEAR_SWIGLU) return op_fail(QW_ERR_ARG, "epilogue " + std::to_string(epi));
+    if (epi == QW_LINEAR_RESID && !resid) return op_fail(QW_ERR_ARG, "RESID needs resid");
+    if (n_out < 1 || t < 1 || k < 8 || k % 8) return op_fail(QW_ERR_SHAPE, "n_out, t >= 1 and k a positive multiple of 8");
+    if (epi == QW_LINEAR_SWIGLU && n_out % 32) return op_fail(QW_ERR_SHAPE, "SWIGLU needs n_out a multiple of 32");
+    if (((uintptr_t)w | (uintptr_t)x) & 15) return op_fail(QW_ERR_ARG, "w and x must be 16-byte aligned");
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return op_fail(QW_ERR_CUDA, "no current device");
+    TcArgs a{};
+    a.M = n_out; a.T = t; a.K = k; a.ksplit = 1;
+    a.out = out; a.ld_out = epi == QW_LINEAR_SWIGLU ? n_out / 2 : n_out;
+    a.resid = resid; a.ld_resid = n_out; a.bias = epi == QW_LINEAR_STORE ? bias : nullptr;
+    cudaError_t e = tc_gemm_launch(w, x, a, epi, 0, sms, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_fail(QW_ERR_CUDA, std::string("linear launch: ") + cudaGetErrorString(e));
     return QW_OK;
 }

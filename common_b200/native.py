@@ -25,7 +25,7 @@ EXPORTS = ("qw_abi_version", "qw_build_info", "qw_get_unique_id", "qw_create", "
            "qw_finalize_weights", "qw_reset", "qw_reserve", "qw_decode_step", "qw_forward_hidden", "qw_prefill",
            "qw_generate", "qw_decode_step_device", "qw_capture_decode", "qw_replay_decode", "qw_synchronize",
            "qw_stream", "qw_last_launch_count", "qw_last_error", "qw_destroy", "qw_profile_decode",
-           "qw_set_device_inputs", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static")
+           "qw_set_device_inputs", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static", "qw_op_linear")
 KERNEL_NAMES = {0: "other", 1: "qkv", 2: "attn", 3: "o_proj", 4: "gate_up", 5: "down", 6: "lm_head"}
 
 
@@ -82,6 +82,7 @@ def load() -> C.CDLL:
         "qw_profile_decode": (I32, [P, I32, PF, PI, I32, PI]),
         "qw_set_device_inputs": (I32, [P, PI, PI, I32]),
         "qw_op_lm_head_argmax": (I32, [P, I32, I32, I32, P, P, C.c_double, I32, P, P, P]),
+        "qw_op_linear": (I32, [P, I32, I32, P, I32, I32, P, P, P, P]),
         "qw_op_lm_head_argmax_static": (I32, [P, I32, I32, I32, P, P, C.c_double, I32, P, P, P]),
     }
     for name, (res, args) in sig.items():
@@ -120,6 +121,18 @@ def op_lm_head_argmax(w_ptr: int, w_dtype: int, vocab: int, dim: int, x_ptr: int
     """qw_op_lm_head_argmax over raw device pointers."""
     st = load().qw_op_lm_head_argmax(w_ptr, w_dtype, vocab, dim, x_ptr, norm_ptr, eps, batch, logits_ptr or None,
                                      argmax_ptr, stream or None)
+    if st:
+        raise QwenError(st, op_error())
+
+
+LINEAR_STORE, LINEAR_RESID, LINEAR_SWIGLU = 0, 1, 2
+
+
+def op_linear(w_ptr: int, n_out: int, k: int, x_ptr: int, t: int, epi: int, bias_ptr: int, resid_ptr: int,
+              out_ptr: int, stream: int = 0) -> None:
+    """qw_op_linear (tcgen05 GEMM) over raw device pointers."""
+    st = load().qw_op_linear(w_ptr, n_out, k, x_ptr, t, epi, bias_ptr or None, resid_ptr or None, out_ptr,
+                             stream or None)
     if st:
         raise QwenError(st, op_error())
 

@@ -212,6 +212,20 @@ qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_t vocab, in
                                const float *norm_w, double eps, int32_t batch, float *logits_out,
                                int32_t *argmax_out, void *stream);
 
+/* Batched projection on the tensor cores (tcgen05/TMEM, TMA-fed): for bf16 W (n_out, k) and bf16 X
+ * (t, k), both row-major, acc(t, f) = sum_j W(f, j) X(t, j) in fp32, then by `epi`:
+ *   QW_LINEAR_STORE   out fp32 (t, n_out) = acc (+ bias[f] when bias is not NULL)
+ *   QW_LINEAR_RESID   out fp32 (t, n_out) = resid (t, n_out) + acc  (out may equal resid)
+ *   QW_LINEAR_SWIGLU  W rows interleaved in blocks of 16 gate rows then 16 up rows;
+ *                     out bf16 (t, n_out/2) = up * silu(gate)
+ * k a multiple of 8, pointers 16-byte aligned, n_out a multiple of 32 for SWIGLU.  Stands in
+ * for LayerFeatures.dense applied to t rows (domain/graph/src/main/java/org/almostrealism/layers/
+ * LayerFeatures.java:785-830) with SequentialBlock.accum (SequentialBlock.java:413-429) and the
+ * SwiGLU product (engine/ml/src/main/java/org/almostrealism/ml/FeedForwardFeatures.java:147-156). */
+enum { QW_LINEAR_STORE = 0, QW_LINEAR_RESID = 1, QW_LINEAR_SWIGLU = 2 };
+qw_status qw_op_linear(const void *w, int32_t n_out, int32_t k, const void *x, int32_t t, int32_t epi,
+                       const float *bias, const float *resid, void *out, void *stream);
+
 /* qw_op_lm_head_argmax with no allocation anywhere: same arguments, results and errors,
  * but its cross-CTA scratch is a fixed 64 KiB array compiled into the library (held on every
  * GPU that loads it until the process exits) instead of memory from cudaMalloc.  For hosts
