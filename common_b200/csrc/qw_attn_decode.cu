@@ -290,7 +290,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         }
         int h = kvh * G + g;
         if (a.nsplit == 1) {
-            a.out[(size_t)b * a.ld_out + (size_t)h * D + j] = O / L;
+            const size_t oi = (size_t)b * a.ld_out + (size_t)h * D + j;
+            if (a.out_bf16) a.out_bf16[oi] = __float2bfloat16_rn(O / L);
+            else a.out[oi] = O / L;
         } else {
             size_t pidx = ((size_t)b * H + h) * a.nsplit + split;
             a.part_o[pidx * D + j] = O;
@@ -335,7 +337,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         float O = 0.f;
 #pragma unroll 4
         for (int s = 0; s < ns_eff; s++) O += sw[g][s] * __ldcg(po + (size_t)s * D);
-        a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + g) * D + j] = O;
+        const size_t oi = (size_t)b * a.ld_out + (size_t)(kvh * G + g) * D + j;
+        if (a.out_bf16) a.out_bf16[oi] = __float2bfloat16_rn(O);
+        else a.out[oi] = O;
     }
     if (tid == 0) a.counters[(size_t)b * Hkv + kvh] = 0u;
 }

@@ -375,12 +375,6 @@ cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int cols, int b
 template <int BN, int EPI>
 cudaError_t launch_bn(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a, int num_sms, cudaStream_t st) {
     auto kfn = tc_gemm_kernel<BN, EPI>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute((const void *)kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes(BN));
-    });
-    if (attr_err != cudaSuccess) return attr_err;
     const int nf = (a.M + kBM - 1) / kBM, nt = (a.T + BN - 1) / BN;
     const int total = nf * nt * a.ksplit;
     const int grid = total < num_sms ? total : num_sms;
@@ -400,6 +394,20 @@ cudaError_t launch_epi(const CUtensorMap &mw, const CUtensorMap &mx, const TcArg
 }
 
 }  // namespace
+
+cudaError_t tc_prepare() {
+    const void *fns[] = {(const void *)tc_gemm_kernel<64, TC_STORE>,  (const void *)tc_gemm_kernel<128, TC_STORE>,
+                         (const void *)tc_gemm_kernel<256, TC_STORE>, (const void *)tc_gemm_kernel<64, TC_RESID>,
+                         (const void *)tc_gemm_kernel<128, TC_RESID>, (const void *)tc_gemm_kernel<256, TC_RESID>,
+                         (const void *)tc_gemm_kernel<64, TC_SWIGLU>, (const void *)tc_gemm_kernel<128, TC_SWIGLU>,
+                         (const void *)tc_gemm_kernel<256, TC_SWIGLU>};
+    const int bns[] = {64, 128, 256, 64, 128, 256, 64, 128, 256};
+    for (int i = 0; i < 9; i++) {
+        cudaError_t e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes(bns[i]));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
 
 int tc_pick_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
 

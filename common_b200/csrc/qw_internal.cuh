@@ -168,6 +168,7 @@ struct AttnArgs {
     unsigned *counters;    // (B, Hkv), zero on entry
     float *out;            // (B, ld_out) attention output, head-major
     int ld_out;
+    __nv_bfloat16 *out_bf16;  // optional: bf16 output (B, ld_out) instead of `out`
 };
 
 }  // namespace qw

@@ -38,6 +38,69 @@ cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, flo
 cudaError_t hold_launch(unsigned long long ns, cudaStream_t st);
 cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cudaStream_t st);
 
+struct NormRowsArgs {
+    float *x;  // (rows, ld_x) fp32 residual stream: read, or written when embed / part is given
+    int ld_x;
+    const float *part;  // optional (rows, ld_part) all-reduced partial added to x (and stored)
+    int ld_part;
+    const __nv_bfloat16 *embed;  // optional (vocab, K) bf16 table: x = embed[tokens[r]] (stored)
+    const int *tokens;
+    const float *w;  // rmsnorm weight (K)
+    float eps;
+    __nv_bfloat16 *out;  // (rows, ld_out) bf16 normalised rows
+    int ld_out;
+    int K;
+};
+
+struct QkvPostArgs {
+    const float *qkv;  // (rows, ld_qkv) fp32: q | k | v of this rank's heads
+    int ld_qkv;
+    const float *qn, *kn;
+    int qk_mode;         // 0 none, 1 whole vector, 2 per head
+    const float *qk_ss;  // optional (rows, 2) global sums of squares (vector mode, tp > 1)
+    int q_total, kv_total;
+    const float2 *freq;
+    const int *slots, *positions;  // per row
+    const int *page_table;
+    int max_pages, page_size, log2_page;
+    void *kcache, *vcache;  // this layer
+    int H, Hkv, d;
+    __nv_bfloat16 *q_out;  // (rows, ld_q) bf16 rotated queries
+    int ld_q;
+};
+
+struct FlashArgs {
+    const __nv_bfloat16 *q;  // (nseq * L, ld_q): sequence b's rows b*L .. b*L+L-1
+    int ld_q;
+    const void *kcache, *vcache;  // this layer, bf16
+    const int *page_table;
+    int max_pages, page_size, log2_page;
+    const int *seq_slots;  // (nseq)
+    int p0, L;             // the chunk covers positions p0 .. p0+L-1 of every sequence
+    int H, Hkv, d;
+    float scale;
+    __nv_bfloat16 *out;  // (nseq * L, ld_out)
+    int ld_out;
+};
+
+struct RowsArgmaxArgs {
+    const float *logits;  // (rows, ld)
+    int ld, n;
+    int idx_offset;
+    int *argmax_out;
+    float *argmax_val;
+    int *next_tokens, *positions;
+    int advance;
+    int *hist;
+    int hist_ld;
+};
+
+cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st);
+cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st);
+cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st);
+cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t st);
+cudaError_t prefill_kernels_prepare();  // opt the row kernels in to their shared memory (once, before capture)
+
 cudaError_t gemv_launch(const GemvArgs &a, int epi, bool bf16, int num_sms, cudaStream_t st);
 cudaError_t attn_decode_launch(const AttnArgs &a, int B, bool kv_bf16, cudaStream_t st);
 

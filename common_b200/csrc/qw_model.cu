@@ -18,6 +18,7 @@
 #include "qw_kernels.h"
 #include "qw_prefill.h"
 #include "qw_ops.h"
+#include "qw_tc.h"
 
 using namespace qw;
 
@@ -319,6 +320,50 @@ qw_status allreduce(qw_model *m, float *buf, size_t n) {
     return QW_OK;
 }
 
+// Tensor-parallel tail: all-gather every rank's (value, index) winner and its logits shard.
+qw_status tp_merge_argmax(qw_model *m, int B, float *logits_out_dev, int *argmax_dev, int *next_tokens, int *positions,
+                          int advance, int *hist, int hist_ld) {
+    NK(ncclAllGather(m->am_val, m->am_val_all, B, ncclFloat, m->comm, m->st));
+    NK(ncclAllGather(m->am_idx, m->am_idx_all, B, ncclInt32, m->comm, m->st));
+    LK(argmax_merge_launch(m->am_val_all, m->am_idx_all, m->tp, B, argmax_dev, next_tokens, positions, advance, hist,
+                           hist_ld, m->st));
+    if (logits_out_dev) {
+        NK(ncclAllGather(m->logits, m->logits_all, (size_t)B * m->Vl, ncclFloat, m->comm, m->st));
+        // logits_all is [rank][b][Vl] -> logits_out_dev [b][V]
+        for (int r = 0; r < m->tp; r++)
+            CK(cudaMemcpy2DAsync(logits_out_dev + (size_t)r * m->Vl, sizeof(float) * m->c.vocab,
+                                 m->logits_all + (size_t)r * B * m->Vl, sizeof(float) * m->Vl, sizeof(float) * m->Vl,
+                                 B, cudaMemcpyDeviceToDevice, m->st));
+    }
+    return QW_OK;
+}
+
+// Final rmsnorm + lm_head + greedy argmax for B <= kGemvMaxB rows x (row b at xin + b * ld_in, plus an
+// optional all-reduced partial), merged across tensor-parallel ranks.
+qw_status lm_head_gemv(qw_model *m, const float *xin, int ld_in, const float *pending, int ld_part, int B,
+                       float *logits_out_dev, int *argmax_dev, int *next_tokens, int *positions, int advance, int *hist,
+                       int hist_ld) {
+    const qw_config &c = m->c;
+    const int D = m->D;
+    const bool tpm = m->tp > 1;
+    GemvArgs g{};
+    g.W = m->lm; g.N = m->Vl; g.K = D; g.B = B; g.xin = xin; g.ld_in = ld_in;
+    if (pending) { g.part = pending; g.ld_part = ld_part; }
+    g.norm_w = m->norm_final; g.eps = (float)c.eps;
+    g.out = tpm ? m->logits : logits_out_dev; g.ld_out = m->Vl;
+    if (tpm && !logits_out_dev) g.out = nullptr;
+    g.part_val = m->am_pval; g.part_idx = m->am_pidx; g.counter = m->am_counter; g.idx_offset = m->v0;
+    if (!tpm) {
+        g.argmax_out = argmax_dev; g.next_tokens = next_tokens; g.positions = positions; g.advance = advance;
+        g.hist = hist; g.hist_ld = hist_ld;
+    } else {
+        g.argmax_out = m->am_idx; g.argmax_val = m->am_val;
+    }
+    LKK(QW_KERNEL_LM_HEAD, gemv_launch(g, EPI_ARGMAX, m->bf16w, m->num_sms, m->st));
+    if (tpm) return tp_merge_argmax(m, B, logits_out_dev, argmax_dev, next_tokens, positions, advance, hist, hist_ld);
+    return QW_OK;
+}
+
 // One forward for B <= 4 rows.  tokens: device token ids (or null when x_in given: fp32 (B, D)).
 qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const int *slots, int *positions, int B,
                       float *logits_out_dev, int *argmax_dev, int *next_tokens, int advance, int *hist, int hist_ld) {
@@ -395,35 +440,138 @@ qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const i
             pending = m->part;
         } else std::swap(xcur, xalt);
     }
-    // ---- final rmsnorm + lm_head + argmax ----
-    GemvArgs g{};
-    g.W = m->lm; g.N = m->Vl; g.K = D; g.B = B; g.xin = xcur; g.ld_in = D;
-    if (pending) { g.part = pending; g.ld_part = D; }
-    g.norm_w = m->norm_final; g.eps = (float)c.eps;
-    g.out = tpm ? m->logits : logits_out_dev; g.ld_out = m->Vl;
-    if (tpm && !logits_out_dev) g.out = nullptr;
-    g.part_val = m->am_pval; g.part_idx = m->am_pidx; g.counter = m->am_counter; g.idx_offset = m->v0;
-    if (!tpm) {
-        g.argmax_out = argmax_dev; g.next_tokens = next_tokens; g.positions = positions; g.advance = advance;
-        g.hist = hist; g.hist_ld = hist_ld;
-    } else {
-        g.argmax_out = m->am_idx; g.argmax_val = m->am_val;
-    }
-    LKK(QW_KERNEL_LM_HEAD, gemv_launch(g, EPI_ARGMAX, m->bf16w, m->num_sms, m->st));
-    if (tpm) {
-        NK(ncclAllGather(m->am_val, m->am_val_all, B, ncclFloat, m->comm, m->st));
-        NK(ncclAllGather(m->am_idx, m->am_idx_all, B, ncclInt32, m->comm, m->st));
-        LK(argmax_merge_launch(m->am_val_all, m->am_idx_all, m->tp, B, argmax_dev, next_tokens, positions, advance, hist,
-                               hist_ld, m->st));
-        if (logits_out_dev) {
-            NK(ncclAllGather(m->logits, m->logits_all, (size_t)B * m->Vl, ncclFloat, m->comm, m->st));
-            // logits_all is [rank][b][Vl] -> logits_out_dev [b][V]
-            for (int r = 0; r < m->tp; r++)
-                CK(cudaMemcpy2DAsync(logits_out_dev + (size_t)r * m->Vl, sizeof(float) * c.vocab,
-                                     m->logits_all + (size_t)r * B * m->Vl, sizeof(float) * m->Vl,
-                                     sizeof(float) * m->Vl, B, cudaMemcpyDeviceToDevice, m->st));
+    return lm_head_gemv(m, xcur, D, pending, D, B, logits_out_dev, argmax_dev, next_tokens, positions, advance, hist,
+                        hist_ld);
+}
+
+// ------------------------------------------------------------------------------------------
+// the batched step on the tensor cores: prefill chunks and decode batches above kGemvMaxB
+// ------------------------------------------------------------------------------------------
+qw_status tc_gemm(qw_model *m, const void *W, const void *X, int M, int T, int K, int epi, void *out, int ld_out,
+                  const float *resid, const float *bias, bool allow_split) {
+    TcArgs a{};
+    const int bn = tc_pick_bn(T);
+    a.M = M; a.T = T; a.K = K;
+    a.ksplit = allow_split ? tc_pick_ksplit(M, T, K, bn, m->num_sms) : 1;
+    a.out = out; a.ld_out = ld_out; a.resid = resid; a.ld_resid = ld_out; a.bias = bias; a.err = m->pf.d_err;
+    if (a.ksplit > 1 && epi == TC_STORE) CK(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)T * ld_out, m->st));
+    LKK(QW_KERNEL_OTHER, tc_gemm_launch(W, X, a, epi, bn, m->num_sms, m->st));
+    return QW_OK;
+}
+
+#define TRY(call)                  \
+    do {                           \
+        qw_status s_ = (call);     \
+        if (s_) return s_;         \
+    } while (0)
+
+// All layers for T token rows (row r: token tokens[r] or hidden x_in row r, at slot row_slot[r] and
+// position row_pos[r]).  prefill: the rows are nseq sequences of L consecutive positions from p0
+// (flash attention); otherwise T single-token sequences (paged decode attention).  Leaves the
+// residual stream in m->xa and, under tensor parallelism, the last all-reduced partial in *pending.
+qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, const int *row_slot, const int *row_pos,
+                    bool prefill, int nseq, int p0, int L, const int *seq_slots, const float **pending_out) {
+    const qw_config &c = m->c;
+    PrefillBuffers &pf = m->pf;
+    const int D = m->D, d = c.head_dim;
+    const bool tpm = m->tp > 1;
+    float *x = m->xa;
+    const float *pending = nullptr;
+    if (x_in) CK(cudaMemcpyAsync(x, x_in, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToDevice, m->st));
+    for (int l = 0; l < c.layers; l++) {
+        Layer &Ly = m->L[l];
+        // ---- residual update + rmsnorm -> bf16 rows ----
+        NormRowsArgs na{};
+        na.x = x; na.ld_x = D; na.part = pending; na.ld_part = D;
+        if (l == 0 && !x_in) { na.embed = (const __nv_bfloat16 *)m->embed; na.tokens = tokens; }
+        na.w = Ly.rms_att; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
+        LK(norm_rows_launch(na, T, m->st));
+        pending = nullptr;
+        // ---- fused QKV projection ----
+        TRY(tc_gemm(m, Ly.w_qkv, pf.act, m->QKVl, T, D, TC_STORE, m->qkv, m->QKVl, nullptr, Ly.b_qkv, true));
+        const float *qk_ss = nullptr;
+        if (tpm && c.qk_norm == QW_QKNORM_VECTOR) {
+            LK(qk_sumsq_launch(m->qkv, m->QKVl, m->Ql, m->KVl, T, pf.row_ss, m->st));
+            TRY(allreduce(m, pf.row_ss, (size_t)T * 2));
+            qk_ss = pf.row_ss;
+        }
+        void *kc = (char *)m->kpool + (size_t)l * m->layer_kv_elems * m->kvsz;
+        void *vc = (char *)m->vpool + (size_t)l * m->layer_kv_elems * m->kvsz;
+        if (prefill) {
+            QkvPostArgs qa{};
+            qa.qkv = m->qkv; qa.ld_qkv = m->QKVl; qa.qn = Ly.qn; qa.kn = Ly.kn; qa.qk_mode = c.qk_norm; qa.qk_ss = qk_ss;
+            qa.q_total = c.heads * d; qa.kv_total = c.kv_heads * d; qa.freq = m->freq;
+            qa.slots = row_slot; qa.positions = row_pos; qa.page_table = m->d_page_table; qa.max_pages = m->max_pages;
+            qa.page_size = m->page_size; qa.log2_page = m->log2_page; qa.kcache = kc; qa.vcache = vc;
+            qa.H = m->Hl; qa.Hkv = m->Hkvl; qa.d = d; qa.q_out = pf.q; qa.ld_q = m->Ql;
+            LK(qkv_post_launch(qa, T, m->bf16kv, m->st));
+            FlashArgs fa{};
+            fa.q = pf.q; fa.ld_q = m->Ql; fa.kcache = kc; fa.vcache = vc; fa.page_table = m->d_page_table;
+            fa.max_pages = m->max_pages; fa.page_size = m->page_size; fa.log2_page = m->log2_page;
+            fa.seq_slots = seq_slots; fa.p0 = p0; fa.L = L; fa.H = m->Hl; fa.Hkv = m->Hkvl; fa.d = d;
+            fa.scale = (float)(1.0 / sqrt((double)d)); fa.out = pf.act; fa.ld_out = m->Ql;
+            LKK(QW_KERNEL_ATTN, flash_prefill_launch(fa, nseq, m->st));
+        } else {
+            AttnArgs a{};
+            a.qkv = m->qkv; a.ld_qkv = m->QKVl; a.qn = Ly.qn; a.kn = Ly.kn; a.qk_mode = c.qk_norm; a.qk_ss = qk_ss;
+            a.q_total = c.heads * d; a.kv_total = c.kv_heads * d; a.freq = m->freq; a.kcache = kc; a.vcache = vc;
+            a.page_table = m->d_page_table; a.max_pages = m->max_pages; a.slots = row_slot; a.positions = row_pos;
+            a.H = m->Hl; a.Hkv = m->Hkvl; a.d = d; a.page_size = m->page_size; a.log2_page = m->log2_page;
+            a.nsplit = choose_nsplit(m, T); a.scale = (float)(1.0 / sqrt((double)d));
+            a.part_o = m->part_o; a.part_ml = m->part_ml; a.counters = m->counters;
+            a.out = nullptr; a.out_bf16 = pf.act; a.ld_out = m->Ql;
+            LKK(QW_KERNEL_ATTN, attn_decode_launch(a, T, m->bf16kv, m->st));
+        }
+        // ---- O projection (+ residual) ----
+        if (tpm) {
+            TRY(tc_gemm(m, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, m->part, D, nullptr, nullptr, true));
+            TRY(allreduce(m, m->part, (size_t)T * D));
+            pending = m->part;
+        } else {
+            TRY(tc_gemm(m, Ly.w_o, pf.act, D, T, m->Ql, TC_RESID, x, D, x, nullptr, true));
+        }
+        // ---- residual update + rmsnorm ----
+        na = NormRowsArgs{};
+        na.x = x; na.ld_x = D; na.part = pending; na.ld_part = D;
+        na.w = Ly.rms_ffn; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
+        LK(norm_rows_launch(na, T, m->st));
+        pending = nullptr;
+        // ---- gate/up + SwiGLU, down (+ residual) ----
+        TRY(tc_gemm(m, Ly.w_gu, pf.act, 2 * m->Fl, T, D, TC_SWIGLU, pf.h, m->Fl, nullptr, nullptr, false));
+        if (tpm) {
+            TRY(tc_gemm(m, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, m->part, D, nullptr, nullptr, true));
+            TRY(allreduce(m, m->part, (size_t)T * D));
+            pending = m->part;
+        } else {
+            TRY(tc_gemm(m, Ly.w_down, pf.h, D, T, m->Fl, TC_RESID, x, D, x, nullptr, true));
         }
     }
+    *pending_out = pending;
+    return QW_OK;
+}
+
+// Decode step for B > kGemvMaxB sequences: batched layers, then rmsnorm + lm_head GEMM + row argmax.
+qw_status tc_decode(qw_model *m, int *tokens, const float *x_in, const int *slots, int *positions, int B,
+                    float *logits_out_dev, int *argmax_dev, int advance, int *hist, int hist_ld) {
+    const float *pending = nullptr;
+    TRY(tc_layers(m, B, tokens, x_in, slots, positions, false, 0, 0, 1, nullptr, &pending));
+    const bool tpm = m->tp > 1;
+    NormRowsArgs na{};
+    na.x = m->xa; na.ld_x = m->D; na.part = pending; na.ld_part = m->D;
+    na.w = m->norm_final; na.eps = (float)m->c.eps; na.out = m->pf.act; na.ld_out = m->D; na.K = m->D;
+    LK(norm_rows_launch(na, B, m->st));
+    float *lg = (!tpm && logits_out_dev) ? logits_out_dev : m->logits;
+    TRY(tc_gemm(m, m->lm, m->pf.act, m->Vl, B, m->D, TC_STORE, lg, m->Vl, nullptr, nullptr, false));
+    RowsArgmaxArgs ra{};
+    ra.logits = lg; ra.ld = m->Vl; ra.n = m->Vl; ra.idx_offset = m->v0;
+    if (!tpm) {
+        ra.argmax_out = argmax_dev; ra.next_tokens = tokens; ra.positions = positions; ra.advance = advance;
+        ra.hist = hist; ra.hist_ld = hist_ld;
+    } else {
+        ra.argmax_out = m->am_idx; ra.argmax_val = m->am_val;
+    }
+    LKK(QW_KERNEL_LM_HEAD, rows_argmax_launch(ra, B, m->st));
+    if (tpm) return tp_merge_argmax(m, B, logits_out_dev, argmax_dev, tokens, positions, advance, hist, hist_ld);
     return QW_OK;
 }
 
@@ -433,6 +581,9 @@ qw_status device_step(qw_model *m, int *tokens, const float *x_in, const int *sl
     if (!m->finalized) return fail(m, QW_ERR_STATE, "weights not finalized");
     if (B < 1 || B > m->B) return fail(m, QW_ERR_SHAPE, "batch %d outside [1,%d]", B, m->B);
     m->launches = 0;
+    if (B > kGemvMaxB && m->pf.tc)
+        return tc_decode(m, tokens, x_in, slots ? slots : m->d_slots, positions, B, logits_dev, argmax_dev, advance,
+                         hist, hist_ld);
     for (int b0 = 0; b0 < B; b0 += kGemvMaxB) {
         int nb = std::min(kGemvMaxB, B - b0);
         const int *sl = slots ? slots + b0 : nullptr;
@@ -495,6 +646,69 @@ qw_status host_step(qw_model *m, const int32_t *tokens, const float *x_in, const
     return QW_OK;
 }
 
+// Prefill on the tensor cores: chunks of up to T rows (batch x chunk positions), flash attention
+// over the paged cache, then the last position's rmsnorm + lm_head + argmax per sequence.
+qw_status tc_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, int batch, int seq_len,
+                     float *logits_out, int32_t *argmax_out) {
+    PrefillBuffers &pf = m->pf;
+    std::vector<int> sl(batch);
+    for (int b = 0; b < batch; b++) {
+        sl[b] = slots ? slots[b] : b;
+        if (sl[b] < 0 || sl[b] >= m->B) return fail(m, QW_ERR_ARG, "slot %d out of range", sl[b]);
+        for (int b2 = 0; b2 < b; b2++)
+            if (sl[b2] == sl[b]) return fail(m, QW_ERR_ARG, "slot %d used twice in one batch", sl[b]);
+        for (int p = 0; p < seq_len; p++) {
+            int t = tokens[(size_t)b * seq_len + p];
+            if (t < 0 || t >= m->c.vocab) return fail(m, QW_ERR_ARG, "token %d outside vocab", t);
+        }
+        TRY(reserve_pages(m, sl[b], seq_len));
+    }
+    const int Lc = std::max(1, std::min(seq_len, m->T / batch));
+    const int Tmax = m->T;
+    int *pin = pf.h_pin;
+    const float *pending = nullptr;
+    int L = 0;
+    m->launches = 0;
+    for (int p0 = 0; p0 < seq_len; p0 += Lc) {
+        L = std::min(Lc, seq_len - p0);
+        const int T = batch * L;
+        CK(cudaStreamSynchronize(m->st));  // the pinned staging of the previous chunk has been consumed
+        for (int b = 0; b < batch; b++) {
+            pin[3 * Tmax + b] = sl[b];
+            for (int i = 0; i < L; i++) {
+                const int r = b * L + i;
+                pin[r] = sl[b];
+                pin[Tmax + r] = p0 + i;
+                pin[2 * Tmax + r] = tokens[(size_t)b * seq_len + p0 + i];
+            }
+        }
+        CK(cudaMemcpyAsync(pf.row_slot, pin, sizeof(int) * (size_t)(3 * Tmax + batch), cudaMemcpyHostToDevice, m->st));
+        TRY(tc_layers(m, T, pf.row_tok, nullptr, pf.row_slot, pf.row_pos, true, batch, p0, L, pf.seq_slots, &pending));
+    }
+    // last position of every sequence: row b*L + L-1 of the final chunk
+    float *dlog = nullptr;
+    if (logits_out) dlog = m->logits_all ? m->logits_all + (size_t)m->tp * m->B * m->Vl : m->logits;
+    const size_t ld = (size_t)L * m->D;
+    for (int b0 = 0; b0 < batch; b0 += kGemvMaxB) {
+        const int nb = std::min(kGemvMaxB, batch - b0);
+        const size_t off = ((size_t)b0 * L + L - 1) * m->D;
+        TRY(lm_head_gemv(m, m->xa + off, (int)ld, pending ? pending + off : nullptr, (int)ld, nb,
+                         dlog ? dlog + (size_t)b0 * m->c.vocab : nullptr, m->d_argmax + b0, nullptr, nullptr, 0,
+                         nullptr, 0));
+    }
+    int *hp = m->h_pin_i + 3 * m->B;
+    CK(cudaMemcpyAsync(hp, m->d_argmax, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
+    if (logits_out)
+        CK(cudaMemcpyAsync(logits_out, dlog, sizeof(float) * (size_t)batch * m->c.vocab, cudaMemcpyDeviceToHost, m->st));
+    int derr = 0;
+    CK(cudaMemcpyAsync(&pin[0], pf.d_err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    derr = pin[0];
+    if (derr) return fail(m, QW_ERR_TIMEOUT, "tensor-core kernel gave up waiting (device error %d)", derr);
+    if (argmax_out) memcpy(argmax_out, hp, sizeof(int) * batch);
+    return QW_OK;
+}
+
 }  // namespace
 
 // ==========================================================================================
@@ -541,6 +755,7 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
     m->log2_page = 0;
     while ((1 << m->log2_page) < m->page_size) m->log2_page++;
     m->dev = device; m->rank = tp_rank; m->tp = tp_size;
+
     m->bf16w = c.weight_dtype == QW_DTYPE_BF16; m->wsz = m->bf16w ? 2 : 4;
     m->bf16kv = c.kv_dtype == QW_DTYPE_BF16; m->kvsz = m->bf16kv ? 2 : 4;
     m->D = c.dim; m->Hl = c.heads / tp_size; m->Hkvl = c.kv_heads / tp_size;
@@ -626,6 +841,10 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
     CK(cudaHostAlloc((void **)&m->h_pin_i, sizeof(int) * 4 * B, cudaHostAllocDefault));
     qw_status s = prefill_alloc(m->pf, c, m->T, m->B, m->Ql, m->KVl, m->Fl, m->D);
     if (s) return fail(m, s, "prefill buffers: %s", cudaGetErrorString(cudaGetLastError()));
+    if (m->pf.tc) {
+        CK(tc_prepare());
+        CK(prefill_kernels_prepare());
+    }
     CK(cudaStreamSynchronize(m->st));
     return QW_OK;
 }
@@ -794,7 +1013,9 @@ qw_status qw_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, i
     if (batch < 1 || batch > m->B || seq_len < 1 || seq_len > m->c.seq_len)
         return fail(m, QW_ERR_SHAPE, "prefill batch %d x %d", batch, seq_len);
     CK(cudaSetDevice(m->dev));
-    // Token-by-token prefill through the decode kernels (the reference's own schedule).
+    if (!m->finalized) return fail(m, QW_ERR_STATE, "weights not finalized");
+    if (m->pf.tc) return tc_prefill(m, tokens, slots, batch, seq_len, logits_out, argmax_out);
+    // Token-by-token prefill through the decode kernels (the reference's own schedule; the fp32 path).
     std::vector<int> tok(batch), pos(batch);
     for (int p = 0; p < seq_len; p++) {
         for (int b = 0; b < batch; b++) { tok[b] = tokens[(size_t)b * seq_len + p]; pos[b] = p; }

@@ -104,6 +104,16 @@ extern "C" qw_status qw_op_linear(const void *w, int32_t n_out, int32_t k, const
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
         return op_fail(QW_ERR_CUDA, "no current device");
+    {
+        static std::mutex mu;
+        static bool prepared[64] = {};
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev < 64 && !prepared[dev]) {
+            cudaError_t e = tc_prepare();
+            if (e != cudaSuccess) return op_fail(QW_ERR_CUDA, std::string("GEMM set-up: ") + cudaGetErrorString(e));
+            prepared[dev] = true;
+        }
+    }
     TcArgs a{};
     a.M = n_out; a.T = t; a.K = k; a.ksplit = 1;
     a.out = out; a.ld_out = epi == QW_LINEAR_SWIGLU ? n_out / 2 : n_out;

@@ -1,0 +1,421 @@
+// qw_prefill.cu -- kernels around the tensor-core projections of prefill and batched decode.
+//
+//   norm_rows     residual stream update (embedding gather for layer 0, plus an all-reduced
+//                 partial under tensor parallelism) and rmsnorm (NormalizationLayerFeatures.java:
+//                 587-603) of every token row into the bf16 operand of the next GEMM;
+//   qkv_post      per token: QK-norm (whole-vector as the reference, AttentionFeatures.java:840-845,
+//                 886-891, or per head), split-half RoPE (RotationFeatures.java:124-170, 189-208),
+//                 the paged KV-cache write (AttentionFeatures.java:823-877) and the bf16 query row;
+//   flash_prefill causal GQA attention of a chunk of prompt positions over the paged cache
+//                 (scores AttentionFeatures.java:531-559, mask :906-917, log-stable softmax
+//                 ActivationFeatures.java:136-142, PV AttentionFeatures.java:572-616) as the
+//                 online-softmax tiling on bf16 mma.sync tensor-core tiles, fp32 accumulation;
+//   rows_argmax   first index of the maximum of each logits row (AggregationFeatures.java:111-121).
+#include "qw_internal.cuh"
+#include "qw_kernels.h"
+#include <float.h>
+#include <limits.h>
+
+namespace qw {
+
+// ------------------------------------------------------------------------------------------
+// norm_rows: one CTA per token row
+// ------------------------------------------------------------------------------------------
+constexpr int kNormThreads = 256;
+constexpr size_t kPrepSmem = 160 * 1024;  // dynamic shared memory the row kernels are opted in to
+
+__global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(NormRowsArgs a) {
+    extern __shared__ __align__(16) float xrow[];
+    __shared__ float red[kNormThreads / 32];
+    const int r = blockIdx.x, K = a.K, tid = threadIdx.x;
+    const __nv_bfloat16 *erow = a.embed ? a.embed + (size_t)a.tokens[r] * K : nullptr;
+    float ss = 0.f;
+    for (int k = tid * 4; k < K; k += kNormThreads * 4) {
+        float4 v;
+        if (erow) {
+            uint2 u = *reinterpret_cast<const uint2 *>(erow + k);
+            v = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+        } else {
+            v = *reinterpret_cast<const float4 *>(a.x + (size_t)r * a.ld_x + k);
+        }
+        if (a.part) {
+            float4 p = *reinterpret_cast<const float4 *>(a.part + (size_t)r * a.ld_part + k);
+            v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+        }
+        if (erow || a.part) *reinterpret_cast<float4 *>(a.x + (size_t)r * a.ld_x + k) = v;
+        *reinterpret_cast<float4 *>(xrow + k) = v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; w++) tot += red[w];
+    const float sc = 1.0f / sqrtf(tot / (float)K + a.eps);
+    for (int k = tid * 4; k < K; k += kNormThreads * 4) {
+        float4 v = *reinterpret_cast<const float4 *>(xrow + k);
+        float4 w = *reinterpret_cast<const float4 *>(a.w + k);
+        uint2 o;
+        o.x = (uint32_t)f2bf_bits(w.x * v.x * sc) | ((uint32_t)f2bf_bits(w.y * v.y * sc) << 16);
+        o.y = (uint32_t)f2bf_bits(w.z * v.z * sc) | ((uint32_t)f2bf_bits(w.w * v.w * sc) << 16);
+        *reinterpret_cast<uint2 *>(a.out + (size_t)r * a.ld_out + k) = o;
+    }
+}
+
+cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
+    if (rows < 1 || a.K % 4) return cudaErrorInvalidValue;
+    size_t smem = sizeof(float) * a.K;
+    if (smem > kPrepSmem) return cudaErrorInvalidValue;
+    norm_rows_kernel<<<rows, kNormThreads, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------
+// qkv_post: one CTA per token row
+// ------------------------------------------------------------------------------------------
+constexpr int kPostThreads = 256;
+
+template <typename KT>
+__global__ void __launch_bounds__(kPostThreads) qkv_post_kernel(QkvPostArgs a) {
+    extern __shared__ __align__(16) float row[];  // q (Ql) | k (KVl) | v (KVl)
+    __shared__ float red[2][kPostThreads / 32];
+    __shared__ float s_sc[2];
+    const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int d = a.d, Ql = a.H * d, KVl = a.Hkv * d, W = Ql + 2 * KVl;
+    const float *src = a.qkv + (size_t)r * a.ld_qkv;
+    float sq = 0.f, sk = 0.f;
+    for (int i = tid; i < W; i += kPostThreads) {
+        float v = src[i];
+        row[i] = v;
+        if (i < Ql) sq += v * v;
+        else if (i < Ql + KVl) sk += v * v;
+    }
+    if (a.qk_mode == 1) {
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        if (lane == 0) { red[0][warp] = sq; red[1][warp] = sk; }
+        __syncthreads();
+        if (tid == 0) {
+            float tq = 0.f, tk = 0.f;
+            for (int w = 0; w < kPostThreads / 32; w++) { tq += red[0][w]; tk += red[1][w]; }
+            if (a.qk_ss) { tq = a.qk_ss[2 * r]; tk = a.qk_ss[2 * r + 1]; }
+            s_sc[0] = 1.0f / sqrtf(tq / (float)a.q_total + 1e-6f);
+            s_sc[1] = 1.0f / sqrtf(tk / (float)a.kv_total + 1e-6f);
+        }
+        __syncthreads();
+        const float scq = s_sc[0], sck = s_sc[1];
+        for (int i = tid; i < Ql + KVl; i += kPostThreads)
+            row[i] = i < Ql ? a.qn[i] * row[i] * scq : a.kn[i - Ql] * row[i] * sck;
+    } else if (a.qk_mode == 2) {
+        __syncthreads();
+        for (int hh = warp; hh < a.H + a.Hkv; hh += kPostThreads / 32) {
+            float *v = row + (size_t)hh * d;
+            const float *w = hh < a.H ? a.qn + (size_t)hh * d : a.kn + (size_t)(hh - a.H) * d;
+            float s = 0.f;
+            for (int i = lane; i < d; i += 32) s += v[i] * v[i];
+            s = warp_sum(s);
+            const float sc = 1.0f / sqrtf(s / (float)d + 1e-6f);
+            for (int i = lane; i < d; i += 32) v[i] = w[i] * v[i] * sc;
+        }
+    }
+    __syncthreads();
+    const int pos = a.positions[r];
+    const int half = d / 2;
+    const float2 *fr = a.freq + (size_t)pos * half;
+    for (int i = tid; i < (a.H + a.Hkv) * half; i += kPostThreads) {
+        const int hh = i / half, f = i % half;
+        float *v = row + (size_t)hh * d;
+        const float2 cs = fr[f];
+        const float x1 = v[f], x2 = v[f + half];
+        v[f] = x1 * cs.x - x2 * cs.y;
+        v[f + half] = x2 * cs.x + x1 * cs.y;
+    }
+    __syncthreads();
+    for (int i = tid; i < Ql; i += kPostThreads) a.q_out[(size_t)r * a.ld_q + i] = __float2bfloat16_rn(row[i]);
+    const int slot = a.slots[r];
+    const int page = a.page_table[(size_t)slot * a.max_pages + (pos >> a.log2_page)];
+    KT *kc = reinterpret_cast<KT *>(a.kcache);
+    KT *vc = reinterpret_cast<KT *>(a.vcache);
+    for (int i = tid; i < KVl; i += kPostThreads) {
+        const int h = i / d, j = i % d;
+        const size_t off = (((size_t)page * a.Hkv + h) * a.page_size + (pos & (a.page_size - 1))) * d + j;
+        Elt<KT>::store(kc + off, row[Ql + i]);
+        Elt<KT>::store(vc + off, row[Ql + KVl + i]);
+    }
+}
+
+cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st) {
+    size_t smem = sizeof(float) * (size_t)(a.H + 2 * a.Hkv) * a.d;
+    auto k16 = qkv_post_kernel<__nv_bfloat16>;
+    auto k32 = qkv_post_kernel<float>;
+    if (smem > kPrepSmem) return cudaErrorInvalidValue;
+    if (kv_bf16) k16<<<rows, kPostThreads, smem, st>>>(a);
+    else k32<<<rows, kPostThreads, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------
+// flash_prefill: grid (query tiles of 64, query heads, sequences), 4 warps x 16 query rows
+// ------------------------------------------------------------------------------------------
+constexpr int kFaRows = 64, kFaKeys = 64, kFaWarps = 4;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    return (uint32_t)f2bf_bits(lo) | ((uint32_t)f2bf_bits(hi) << 16);
+}
+
+// byte offset of (row, 16-byte chunk) in a [rows][D] bf16 tile, chunks XOR-swizzled by row
+template <int D>
+__device__ __forceinline__ uint32_t fa_off(int row, int chunk) {
+    return (uint32_t)(row * D * 2 + ((chunk ^ (row & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFaWarps * 32) flash_prefill_kernel(FlashArgs a) {
+    constexpr int CH = D / 8;  // 16-byte chunks per row
+    extern __shared__ __align__(128) uint8_t fsm[];
+    uint8_t *sK = fsm;                      // [2][64][D]
+    uint8_t *sV = fsm + 2 * kFaKeys * D * 2;  // [2][64][D]
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int G = a.H / a.Hkv, kvh = h / G;
+    const int q0 = qt * kFaRows;  // first query row of the tile within this sequence's chunk
+    if (q0 >= a.L) return;
+    const int slot = a.seq_slots[b];
+    const int *ptab = a.page_table + (size_t)slot * a.max_pages;
+    const int qpos0 = a.p0 + q0;                              // position of the tile's first query
+    const int qlast = a.p0 + min(a.L, q0 + kFaRows) - 1;      // position of its last query
+    const int nkt = qlast / kFaKeys + 1;                      // key tiles covering [0, qlast]
+    const __nv_bfloat16 *kc = reinterpret_cast<const __nv_bfloat16 *>(a.kcache);
+    const __nv_bfloat16 *vc = reinterpret_cast<const __nv_bfloat16 *>(a.vcache);
+
+    auto load_tile = [&](int kt, int buf) {
+        const uint32_t bk = smem_addr(sK + buf * kFaKeys * D * 2), bv = smem_addr(sV + buf * kFaKeys * D * 2);
+        for (int i = tid; i < kFaKeys * CH; i += kFaWarps * 32) {
+            const int r = i / CH, c = i % CH;
+            const int pos = kt * kFaKeys + r;
+            const bool ok = pos <= qlast;
+            const int page = ok ? ptab[pos >> a.log2_page] : 0;
+            const size_t off = (((size_t)page * a.Hkv + kvh) * a.page_size + (pos & (a.page_size - 1))) * D + c * 8;
+            cp_async16(bk + fa_off<D>(r, c), ok ? kc + off : kc, ok ? 16 : 0);
+            cp_async16(bv + fa_off<D>(r, c), ok ? vc + off : vc, ok ? 16 : 0);
+        }
+        cp_async_commit();
+    };
+    load_tile(0, 0);
+
+    // this warp's 16 query rows as A fragments (direct global loads, rows past the chunk are zero)
+    uint32_t qa[D / 16][4];
+    const int r_lo = q0 + warp * 16 + g, r_hi = r_lo + 8;
+    {
+        const __nv_bfloat16 *qb = a.q + ((size_t)b * a.L) * a.ld_q + (size_t)h * D;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; kk++) {
+            const int c0 = kk * 16 + 2 * t4;
+            qa[kk][0] = r_lo < a.L ? *reinterpret_cast<const uint32_t *>(qb + (size_t)r_lo * a.ld_q + c0) : 0u;
+            qa[kk][1] = r_hi < a.L ? *reinterpret_cast<const uint32_t *>(qb + (size_t)r_hi * a.ld_q + c0) : 0u;
+            qa[kk][2] = r_lo < a.L ? *reinterpret_cast<const uint32_t *>(qb + (size_t)r_lo * a.ld_q + c0 + 8) : 0u;
+            qa[kk][3] = r_hi < a.L ? *reinterpret_cast<const uint32_t *>(qb + (size_t)r_hi * a.ld_q + c0 + 8) : 0u;
+        }
+    }
+    const int pos_lo = a.p0 + r_lo, pos_hi = a.p0 + r_hi;
+    const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
+
+    float o[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+
+    for (int kt = 0; kt < nkt; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nkt) {
+            load_tile(kt + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint32_t bk = smem_addr(sK + buf * kFaKeys * D * 2), bv = smem_addr(sV + buf * kFaKeys * D * 2);
+        // ---- S = Q K^T (16 x 64 per warp) ----
+        float s[kFaKeys / 8][4];
+#pragma unroll
+        for (int j = 0; j < kFaKeys / 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; kk++) {
+#pragma unroll
+            for (int nj = 0; nj < kFaKeys / 16; nj++) {
+                const int i = lane >> 3;
+                const int key = nj * 16 + (i >> 1) * 8 + (lane & 7);
+                const int ch = kk * 2 + (i & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(bk + fa_off<D>(key, ch), b0, b1, b2, b3);
+                mma_bf16(s[2 * nj], qa[kk], b0, b1);
+                mma_bf16(s[2 * nj + 1], qa[kk], b2, b3);
+            }
+        }
+        // ---- causal mask + online softmax ----
+        const int kbase = kt * kFaKeys;
+        float mx_lo = m_lo, mx_hi = m_hi;
+#pragma unroll
+        for (int j = 0; j < kFaKeys / 8; j++) {
+            const int k0 = kbase + j * 8 + 2 * t4;
+            s[j][0] = k0 <= pos_lo ? s[j][0] * sl2 : -INFINITY;
+            s[j][1] = k0 + 1 <= pos_lo ? s[j][1] * sl2 : -INFINITY;
+            s[j][2] = k0 <= pos_hi ? s[j][2] * sl2 : -INFINITY;
+            s[j][3] = k0 + 1 <= pos_hi ? s[j][3] * sl2 : -INFINITY;
+            mx_lo = fmaxf(mx_lo, fmaxf(s[j][0], s[j][1]));
+            mx_hi = fmaxf(mx_hi, fmaxf(s[j][2], s[j][3]));
+        }
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+            mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+        }
+        const float base_lo = mx_lo == -INFINITY ? 0.f : mx_lo, base_hi = mx_hi == -INFINITY ? 0.f : mx_hi;
+        const float al_lo = exp2f(m_lo - base_lo), al_hi = exp2f(m_hi - base_hi);
+        m_lo = mx_lo; m_hi = mx_hi;
+        float sum_lo = 0.f, sum_hi = 0.f;
+#pragma unroll
+        for (int j = 0; j < kFaKeys / 8; j++) {
+            s[j][0] = exp2f(s[j][0] - base_lo); s[j][1] = exp2f(s[j][1] - base_lo);
+            s[j][2] = exp2f(s[j][2] - base_hi); s[j][3] = exp2f(s[j][3] - base_hi);
+            sum_lo += s[j][0] + s[j][1];
+            sum_hi += s[j][2] + s[j][3];
+        }
+        l_lo = l_lo * al_lo + sum_lo;
+        l_hi = l_hi * al_hi + sum_hi;
+#pragma unroll
+        for (int j = 0; j < D / 8; j++) {
+            o[j][0] *= al_lo; o[j][1] *= al_lo; o[j][2] *= al_hi; o[j][3] *= al_hi;
+        }
+        // ---- O += P V ----
+#pragma unroll
+        for (int kk = 0; kk < kFaKeys / 16; kk++) {
+            uint32_t pa[4];
+            pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int nj = 0; nj < D / 16; nj++) {
+                const int i = lane >> 3;
+                const int key = kk * 16 + (i & 1) * 8 + (lane & 7);
+                const int ch = nj * 2 + (i >> 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(bv + fa_off<D>(key, ch), b0, b1, b2, b3);
+                mma_bf16(o[2 * nj], pa, b0, b1);
+                mma_bf16(o[2 * nj + 1], pa, b2, b3);
+            }
+        }
+        __syncthreads();  // this buffer is refilled by the next iteration's prefetch
+    }
+    // ---- normalise and store ----
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+        l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+        l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+    }
+    const float inv_lo = l_lo > 0.f ? 1.0f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.0f / l_hi : 0.f;
+    __nv_bfloat16 *ob = a.out + ((size_t)b * a.L) * a.ld_out + (size_t)h * D;
+#pragma unroll
+    for (int j = 0; j < D / 8; j++) {
+        const int c = j * 8 + 2 * t4;
+        if (r_lo < a.L) *reinterpret_cast<uint32_t *>(ob + (size_t)r_lo * a.ld_out + c) = pack_bf16(o[j][0] * inv_lo, o[j][1] * inv_lo);
+        if (r_hi < a.L) *reinterpret_cast<uint32_t *>(ob + (size_t)r_hi * a.ld_out + c) = pack_bf16(o[j][2] * inv_hi, o[j][3] * inv_hi);
+    }
+}
+
+cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st) {
+    dim3 grid((a.L + kFaRows - 1) / kFaRows, a.H, nseq);
+    if (a.d == 128) {
+        const size_t smem = 4 * kFaKeys * 128 * 2;
+        flash_prefill_kernel<128><<<grid, kFaWarps * 32, smem, st>>>(a);
+    } else if (a.d == 64) {
+        flash_prefill_kernel<64><<<grid, kFaWarps * 32, 4 * kFaKeys * 64 * 2, st>>>(a);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------
+// rows_argmax: one CTA per logits row; first index of the maximum
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) rows_argmax_kernel(RowsArgmaxArgs a) {
+    __shared__ float sv[16];
+    __shared__ int si[16];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const float *row = a.logits + (size_t)b * a.ld;
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int i = tid; i < a.n; i += blockDim.x) {
+        const float v = row[i];
+        if (v > bv) { bv = v; bi = i; }  // increasing i per thread: strict > keeps the first
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((tid & 31) == 0) { sv[tid >> 5] = bv; si[tid >> 5] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        bv = sv[0]; bi = si[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        const int gidx = bi + a.idx_offset;
+        if (a.argmax_val) a.argmax_val[b] = bv;
+        if (a.argmax_out) a.argmax_out[b] = gidx;
+        if (a.hist) a.hist[(size_t)b * a.hist_ld + a.positions[b] + 1] = gidx;
+        if (a.advance) {
+            a.next_tokens[b] = gidx;
+            a.positions[b] += 1;
+        }
+    }
+}
+
+cudaError_t prefill_kernels_prepare() {
+    const void *fns[] = {(const void *)norm_rows_kernel, (const void *)qkv_post_kernel<__nv_bfloat16>,
+                         (const void *)qkv_post_kernel<float>, (const void *)flash_prefill_kernel<128>,
+                         (const void *)flash_prefill_kernel<64>};
+    for (const void *f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t st) {
+    rows_argmax_kernel<<<rows, 512, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace qw

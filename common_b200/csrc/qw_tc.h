@@ -37,6 +37,9 @@ struct TcArgs {
 cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int epi, int bn, int num_sms,
                            cudaStream_t st);
 
+// Opt every GEMM variant in to its shared memory (once per device, outside of stream capture).
+cudaError_t tc_prepare();
+
 // K ranges per tile that fill the GPU for a skinny (decode) problem; 1 for large T.
 int tc_pick_ksplit(int M, int T, int K, int bn, int num_sms);
 int tc_pick_bn(int T);
