@@ -129,6 +129,114 @@ def run_reference(args):
     return 0
 
 
+
+def prefill_flops(g, nseq, L):
+    D, F = g["dim"], g["hidden_dim"]
+    Q, KV = g["heads"] * g["head_dim"], g["kv_heads"] * g["head_dim"]
+    linear = (Q + 2 * KV) * D + D * Q + 2 * F * D + D * F
+    lin = 2.0 * linear * g["layers"] * nseq * L
+    attn = 2.0 * L * L * g["head_dim"] * g["heads"] * g["layers"] * nseq  # causal QK^T + PV
+    return lin + attn, lin, attn
+
+
+def run_batched(args, rank, world, local, nid, peaks):
+    """prefill of 8 x 4096 tokens on the tensor cores, then batch-64 decode at 4096
+    context (the 64 sequences are prefilled in chunks of 32768 tokens first)."""
+    import numpy as np
+    import torch
+    from common_b200 import native
+    g = GEOM_8B
+    NSEQ, L, B = args.prefill_seqs, args.prefill_len, args.decode_batch
+    steps = args.batch_steps
+    seq_len = L + 3 + steps + 8
+    cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
+                             g["vocab"], seq_len, False, native.QKNORM_VECTOR, False, native.DTYPE_BF16,
+                             native.DTYPE_BF16, B, NSEQ * L)
+    m = native.NativeModel(cfg, local, rank, world, nid)
+    m.init_synthetic(0, 0.02)
+    m.finalize()
+    stream = torch.cuda.ExternalStream(m.stream)
+    rng = np.random.default_rng(1)
+    prompts = rng.integers(0, g["vocab"], (B, L)).astype(np.int32)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    # ---- prefill NSEQ x L (warm-up once, then timed repeats; each repeat rewrites the same slots) ----
+    m.prefill(prompts[:NSEQ], want_logits=False)
+    times = []
+    for _ in range(args.prefill_reps):
+        sync_all()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.prefill(prompts[:NSEQ], want_logits=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    pms = min(times) if world == 1 else max(times)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([pms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pms = float(t.item())
+    fl, lin, att = prefill_flops(g, NSEQ, L)
+    tf = fl / (pms * 1e-3) / 1e12
+    peak_tf = peaks.get("bf16_tflops", 1590.0)
+    pd, pk = None, None
+    prefill = {"tok_s": NSEQ * L / (pms * 1e-3), "ms": pms, "seqs": NSEQ, "seq_len": L, "flops": fl,
+               "tflops": tf, "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peak_tf, "unit": "TFLOP/s",
+                                          "frac": tf / world / peak_tf, "per": "GPU",
+                                          "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback"},
+               "flops_split": {"linear": lin, "attention_causal": att, "lm_head": "last position only"},
+               "timing": "qw_prefill through the host API (tokens from host memory), CUDA events, best of "
+                         f"{args.prefill_reps}" if world == 1 else "max over ranks"}
+
+    # ---- batch-B decode at context L: prefill the remaining slots, capture, replay ----
+    for c0 in range(NSEQ, B, NSEQ):
+        m.prefill(prompts[c0:c0 + NSEQ], slots=np.arange(c0, min(B, c0 + NSEQ), dtype=np.int32), want_logits=False)
+    for b in range(B):
+        m.reserve(b, seq_len)
+    dt = torch.tensor(rng.integers(0, g["vocab"], B), dtype=torch.int32, device="cuda")
+    dp = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    ds = torch.arange(B, dtype=torch.int32, device="cuda")
+    dam = torch.zeros(B, dtype=torch.int32, device="cuda")
+    m.capture_decode(dt.data_ptr(), ds.data_ptr(), dp.data_ptr(), B, 0, dam.data_ptr())
+    launches = m.last_launch_count
+    m.replay_decode(3)
+    sync_all()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    m.replay_decode(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([dms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dms = float(t.item())
+    ctx_mid = L + 3 + steps // 2
+    step_bytes = sum(v for k, v in weight_bytes(g, world).items() if k in ("layers_total", "lm_head")) + \
+        B * kv_bytes_per_token(g, ctx_mid, world)
+    gbs = step_bytes / (dms / steps * 1e-3) / 1e9
+    peak = peaks.get("hbm_gbs", 6650.0)
+    # per-kernel split of one eager step
+    m.set_device_inputs(dt.cpu().numpy(), dp.cpu().numpy())
+    d, k = m.profile_decode(B)
+    kern = {}
+    for x, kk in zip(d, k):
+        kern[native.KERNEL_NAMES[int(kk)]] = kern.get(native.KERNEL_NAMES[int(kk)], 0.0) + float(x)
+    decode = {"tok_s": B * steps / (dms * 1e-3), "ms_per_step": dms / steps, "batch": B, "context": [L + 3, L + 3 + steps],
+              "steps": steps, "launches_per_step": launches,
+              "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                           "bytes_per_step": step_bytes, "per": "GPU" if world == 1 else "rank"},
+              "kernel_ms_per_step": kern}
+    m.close()
+    return {"prefill": prefill, "decode_b%d" % B: decode}
+
 # ----------------------------------------------------------------------------------- GPU arm
 def run_ours(args):
     import numpy as np
@@ -242,10 +350,14 @@ def run_ours(args):
                "d2h_bytes_per_step": 4 * B, "steps": e2e_steps,
                "api": "qw_decode_step (host token/position/slot in, host argmax out)"}
 
+    m.close()
+    torch.cuda.empty_cache()
+    batched = None
+    if not args.no_batched:
+        batched = run_batched(args, rank, world, local, nid, peaks)
+        torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        m.close()
-        torch.cuda.empty_cache()
         tok_s, dts, cores = cpu_sample(args.cpu_samples, 2)
         cpu = {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port",
                "sample": f"oracle port fp32 at the 8B geometry (layer weights shared), {args.cpu_samples} samples of "
@@ -267,6 +379,8 @@ def run_ours(args):
                              "step_gbs": step_gbs, "step_frac": step_gbs / peak},
                 "kernel_ms_per_step": tot, "gpu_launches": launches_per_step * args.steps,
                 "launches_per_step": launches_per_step, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu}
+        if batched:
+            line.update(batched)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -280,7 +394,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--cpu-samples", type=int, default=72)
+    ap.add_argument("--cpu-samples", type=int, default=1080)
+    ap.add_argument("--no-batched", action="store_true", help="skip the prefill / batch-64 decode measurements")
+    ap.add_argument("--prefill-seqs", type=int, default=8)
+    ap.add_argument("--prefill-len", type=int, default=4096)
+    ap.add_argument("--prefill-reps", type=int, default=3)
+    ap.add_argument("--decode-batch", type=int, default=64)
+    ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt-len", type=int, default=PROMPT, help="shorter prompts for profiler runs")
     args = ap.parse_args()

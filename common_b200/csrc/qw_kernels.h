@@ -83,6 +83,22 @@ struct FlashArgs {
     int ld_out;
 };
 
+struct FlashDecodeArgs {
+    const __nv_bfloat16 *q;  // (B, ld_q) rotated queries (this rank's heads)
+    int ld_q;
+    const void *kcache, *vcache;  // this layer, bf16; the current position already written
+    const int *page_table;
+    int max_pages, page_size, log2_page;
+    const int *slots, *positions;  // (B)
+    int H, Hkv, d;
+    int nsplit;  // context splits (<= 64), merged by the last CTA of each (sequence, KV head)
+    float scale;
+    float *part_o, *part_ml;  // (B, H, nsplit, d), (B, H, nsplit, 2)
+    unsigned *counters;       // (B, Hkv), zero on entry, reset on exit
+    __nv_bfloat16 *out;       // (B, ld_out)
+    int ld_out;
+};
+
 struct RowsArgmaxArgs {
     const float *logits;  // (rows, ld)
     int ld, n;
@@ -99,6 +115,7 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st);
 cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st);
 cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st);
 cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t st);
+cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st);
 cudaError_t prefill_kernels_prepare();  // opt the row kernels in to their shared memory (once, before capture)
 
 cudaError_t gemv_launch(const GemvArgs &a, int epi, bool bf16, int num_sms, cudaStream_t st);

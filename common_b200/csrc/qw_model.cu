@@ -315,6 +315,16 @@ int choose_nsplit(qw_model *m, int B) {
     return std::max(ns, 1);
 }
 
+// context splits of the tensor-core decode attention: about four CTAs per SM, at most one split per
+// 64-key tile of the longest possible context
+int choose_flash_split(qw_model *m, int B) {
+    const int per = B * m->Hkvl;
+    int ns = (4 * m->num_sms + per - 1) / per;
+    ns = std::min(ns, (m->c.seq_len + 63) / 64);
+    ns = std::min(ns, m->maxsplit);
+    return std::max(ns, 1);
+}
+
 qw_status allreduce(qw_model *m, float *buf, size_t n) {
     NK(ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, m->comm, m->st));
     return QW_OK;
@@ -447,15 +457,15 @@ qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const i
 // ------------------------------------------------------------------------------------------
 // the batched step on the tensor cores: prefill chunks and decode batches above kGemvMaxB
 // ------------------------------------------------------------------------------------------
-qw_status tc_gemm(qw_model *m, const void *W, const void *X, int M, int T, int K, int epi, void *out, int ld_out,
-                  const float *resid, const float *bias, bool allow_split) {
+qw_status tc_gemm(qw_model *m, int kind, const void *W, const void *X, int M, int T, int K, int epi, void *out,
+                  int ld_out, const float *resid, const float *bias, bool allow_split) {
     TcArgs a{};
     const int bn = tc_pick_bn(T);
     a.M = M; a.T = T; a.K = K;
     a.ksplit = allow_split ? tc_pick_ksplit(M, T, K, bn, m->num_sms) : 1;
     a.out = out; a.ld_out = ld_out; a.resid = resid; a.ld_resid = ld_out; a.bias = bias; a.err = m->pf.d_err;
     if (a.ksplit > 1 && epi == TC_STORE) CK(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)T * ld_out, m->st));
-    LKK(QW_KERNEL_OTHER, tc_gemm_launch(W, X, a, epi, bn, m->num_sms, m->st));
+    LKK(kind, tc_gemm_launch(W, X, a, epi, bn, m->num_sms, m->st));
     return QW_OK;
 }
 
@@ -488,7 +498,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         LK(norm_rows_launch(na, T, m->st));
         pending = nullptr;
         // ---- fused QKV projection ----
-        TRY(tc_gemm(m, Ly.w_qkv, pf.act, m->QKVl, T, D, TC_STORE, m->qkv, m->QKVl, nullptr, Ly.b_qkv, true));
+        TRY(tc_gemm(m, QW_KERNEL_QKV, Ly.w_qkv, pf.act, m->QKVl, T, D, TC_STORE, m->qkv, m->QKVl, nullptr, Ly.b_qkv, true));
         const float *qk_ss = nullptr;
         if (tpm && c.qk_norm == QW_QKNORM_VECTOR) {
             LK(qk_sumsq_launch(m->qkv, m->QKVl, m->Ql, m->KVl, T, pf.row_ss, m->st));
@@ -497,7 +507,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         }
         void *kc = (char *)m->kpool + (size_t)l * m->layer_kv_elems * m->kvsz;
         void *vc = (char *)m->vpool + (size_t)l * m->layer_kv_elems * m->kvsz;
-        if (prefill) {
+        {
             QkvPostArgs qa{};
             qa.qkv = m->qkv; qa.ld_qkv = m->QKVl; qa.qn = Ly.qn; qa.kn = Ly.kn; qa.qk_mode = c.qk_norm; qa.qk_ss = qk_ss;
             qa.q_total = c.heads * d; qa.kv_total = c.kv_heads * d; qa.freq = m->freq;
@@ -505,6 +515,8 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             qa.page_size = m->page_size; qa.log2_page = m->log2_page; qa.kcache = kc; qa.vcache = vc;
             qa.H = m->Hl; qa.Hkv = m->Hkvl; qa.d = d; qa.q_out = pf.q; qa.ld_q = m->Ql;
             LK(qkv_post_launch(qa, T, m->bf16kv, m->st));
+        }
+        if (prefill) {
             FlashArgs fa{};
             fa.q = pf.q; fa.ld_q = m->Ql; fa.kcache = kc; fa.vcache = vc; fa.page_table = m->d_page_table;
             fa.max_pages = m->max_pages; fa.page_size = m->page_size; fa.log2_page = m->log2_page;
@@ -512,23 +524,22 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             fa.scale = (float)(1.0 / sqrt((double)d)); fa.out = pf.act; fa.ld_out = m->Ql;
             LKK(QW_KERNEL_ATTN, flash_prefill_launch(fa, nseq, m->st));
         } else {
-            AttnArgs a{};
-            a.qkv = m->qkv; a.ld_qkv = m->QKVl; a.qn = Ly.qn; a.kn = Ly.kn; a.qk_mode = c.qk_norm; a.qk_ss = qk_ss;
-            a.q_total = c.heads * d; a.kv_total = c.kv_heads * d; a.freq = m->freq; a.kcache = kc; a.vcache = vc;
-            a.page_table = m->d_page_table; a.max_pages = m->max_pages; a.slots = row_slot; a.positions = row_pos;
-            a.H = m->Hl; a.Hkv = m->Hkvl; a.d = d; a.page_size = m->page_size; a.log2_page = m->log2_page;
-            a.nsplit = choose_nsplit(m, T); a.scale = (float)(1.0 / sqrt((double)d));
-            a.part_o = m->part_o; a.part_ml = m->part_ml; a.counters = m->counters;
-            a.out = nullptr; a.out_bf16 = pf.act; a.ld_out = m->Ql;
-            LKK(QW_KERNEL_ATTN, attn_decode_launch(a, T, m->bf16kv, m->st));
+            FlashDecodeArgs fd{};
+            fd.q = pf.q; fd.ld_q = m->Ql; fd.kcache = kc; fd.vcache = vc; fd.page_table = m->d_page_table;
+            fd.max_pages = m->max_pages; fd.page_size = m->page_size; fd.log2_page = m->log2_page;
+            fd.slots = row_slot; fd.positions = row_pos; fd.H = m->Hl; fd.Hkv = m->Hkvl; fd.d = d;
+            fd.nsplit = choose_flash_split(m, T); fd.scale = (float)(1.0 / sqrt((double)d));
+            fd.part_o = m->part_o; fd.part_ml = m->part_ml; fd.counters = m->counters;
+            fd.out = pf.act; fd.ld_out = m->Ql;
+            LKK(QW_KERNEL_ATTN, flash_decode_launch(fd, T, m->st));
         }
         // ---- O projection (+ residual) ----
         if (tpm) {
-            TRY(tc_gemm(m, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, m->part, D, nullptr, nullptr, true));
+            TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, m->part, D, nullptr, nullptr, true));
             TRY(allreduce(m, m->part, (size_t)T * D));
             pending = m->part;
         } else {
-            TRY(tc_gemm(m, Ly.w_o, pf.act, D, T, m->Ql, TC_RESID, x, D, x, nullptr, true));
+            TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_RESID, x, D, x, nullptr, true));
         }
         // ---- residual update + rmsnorm ----
         na = NormRowsArgs{};
@@ -537,13 +548,13 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         LK(norm_rows_launch(na, T, m->st));
         pending = nullptr;
         // ---- gate/up + SwiGLU, down (+ residual) ----
-        TRY(tc_gemm(m, Ly.w_gu, pf.act, 2 * m->Fl, T, D, TC_SWIGLU, pf.h, m->Fl, nullptr, nullptr, false));
+        TRY(tc_gemm(m, QW_KERNEL_GATE_UP, Ly.w_gu, pf.act, 2 * m->Fl, T, D, TC_SWIGLU, pf.h, m->Fl, nullptr, nullptr, false));
         if (tpm) {
-            TRY(tc_gemm(m, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, m->part, D, nullptr, nullptr, true));
+            TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, m->part, D, nullptr, nullptr, true));
             TRY(allreduce(m, m->part, (size_t)T * D));
             pending = m->part;
         } else {
-            TRY(tc_gemm(m, Ly.w_down, pf.h, D, T, m->Fl, TC_RESID, x, D, x, nullptr, true));
+            TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_RESID, x, D, x, nullptr, true));
         }
     }
     *pending_out = pending;
@@ -561,7 +572,7 @@ qw_status tc_decode(qw_model *m, int *tokens, const float *x_in, const int *slot
     na.w = m->norm_final; na.eps = (float)m->c.eps; na.out = m->pf.act; na.ld_out = m->D; na.K = m->D;
     LK(norm_rows_launch(na, B, m->st));
     float *lg = (!tpm && logits_out_dev) ? logits_out_dev : m->logits;
-    TRY(tc_gemm(m, m->lm, m->pf.act, m->Vl, B, m->D, TC_STORE, lg, m->Vl, nullptr, nullptr, false));
+    TRY(tc_gemm(m, QW_KERNEL_LM_HEAD, m->lm, m->pf.act, m->Vl, B, m->D, TC_STORE, lg, m->Vl, nullptr, nullptr, false));
     RowsArgmaxArgs ra{};
     ra.logits = lg; ra.ld = m->Vl; ra.n = m->Vl; ra.idx_offset = m->v0;
     if (!tpm) {

@@ -159,6 +159,7 @@ cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaSt
 // flash_prefill: grid (query tiles of 64, query heads, sequences), 4 warps x 16 query rows
 // ------------------------------------------------------------------------------------------
 constexpr int kFaRows = 64, kFaKeys = 64, kFaWarps = 4;
+constexpr int kFaMaxSplit = 64;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -365,6 +366,240 @@ cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st) 
     return cudaGetLastError();
 }
 
+
+// ------------------------------------------------------------------------------------------
+// flash_decode: one query token per sequence, the G query heads of a KV head as the rows of
+// one 16-row mma tile.  Grid (splits of the context, KV heads, sequences), 4 warps; every
+// 64-key tile is staged by cp.async (3 stages) and each warp takes 16 of its keys with its own
+// online-softmax state; warps, then splits (last CTA of each sequence / KV head), are merged.
+// ------------------------------------------------------------------------------------------
+constexpr int kFdStages = 3;
+
+template <int D, int G>
+__global__ void __launch_bounds__(kFaWarps * 32) flash_decode_kernel(FlashDecodeArgs a) {
+    constexpr int CH = D / 8;
+    constexpr int TILE_BYTES = kFaKeys * D * 2;
+    extern __shared__ __align__(128) uint8_t fsm[];
+    __shared__ float wm[kFaWarps][16], wl[kFaWarps][16];
+    __shared__ float sw[G][kFaMaxSplit];
+    __shared__ int s_last;
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int slot = a.slots ? a.slots[b] : b;
+    const int pos = a.positions[b];
+    const int n = pos + 1;
+    const int ntile_all = (n + kFaKeys - 1) / kFaKeys;
+    const int tiles_per = (ntile_all + a.nsplit - 1) / a.nsplit;
+    const int kt0 = split * tiles_per, kt1 = min(ntile_all, kt0 + tiles_per);
+    const int *ptab = a.page_table + (size_t)slot * a.max_pages;
+    const __nv_bfloat16 *kc = reinterpret_cast<const __nv_bfloat16 *>(a.kcache);
+    const __nv_bfloat16 *vc = reinterpret_cast<const __nv_bfloat16 *>(a.vcache);
+    const int H = a.H, Hkv = a.Hkv;
+
+    auto load_tile = [&](int kt, int st) {
+        const uint32_t bk = smem_addr(fsm + st * 2 * TILE_BYTES), bv = bk + TILE_BYTES;
+        for (int i = tid; i < kFaKeys * CH; i += kFaWarps * 32) {
+            const int r = i / CH, c = i % CH;
+            const int p = kt * kFaKeys + r;
+            const bool ok = p < n;
+            const int page = ok ? ptab[p >> a.log2_page] : 0;
+            const size_t off = (((size_t)page * Hkv + kvh) * a.page_size + (p & (a.page_size - 1))) * D + c * 8;
+            cp_async16(bk + fa_off<D>(r, c), ok ? kc + off : kc, ok ? 16 : 0);
+            cp_async16(bv + fa_off<D>(r, c), ok ? vc + off : vc, ok ? 16 : 0);
+        }
+    };
+
+    float o[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+
+    if (kt0 < kt1) {
+        // prologue: the first stages (the KV rows written by earlier kernels)
+#pragma unroll
+        for (int i = 0; i < kFdStages - 1; i++) {
+            if (kt0 + i < kt1) load_tile(kt0 + i, i);
+            cp_async_commit();
+        }
+        // this warp's query rows: head kvh*G + row for row < G
+        uint32_t qa[D / 16][4];
+        {
+            const __nv_bfloat16 *qb = a.q + (size_t)b * a.ld_q + (size_t)kvh * G * D;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; kk++) {
+                const int c0 = kk * 16 + 2 * t4;
+                qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t *>(qb + (size_t)g * D + c0) : 0u;
+                qa[kk][2] = g < G ? *reinterpret_cast<const uint32_t *>(qb + (size_t)g * D + c0 + 8) : 0u;
+                qa[kk][1] = 0u;  // rows 8..15 are padding (G <= 8)
+                qa[kk][3] = 0u;
+            }
+        }
+        const float sl2 = a.scale * 1.4426950408889634f;
+        for (int kt = kt0; kt < kt1; kt++) {
+            const int st = (kt - kt0) % kFdStages;
+            if (kt + kFdStages - 1 < kt1) load_tile(kt + kFdStages - 1, (kt - kt0 + kFdStages - 1) % kFdStages);
+            cp_async_commit();
+            cp_async_wait<kFdStages - 1>();
+            __syncthreads();
+            const uint32_t bk = smem_addr(fsm + st * 2 * TILE_BYTES), bv = bk + TILE_BYTES;
+            float s[2][4];
+            s[0][0] = s[0][1] = s[0][2] = s[0][3] = 0.f;
+            s[1][0] = s[1][1] = s[1][2] = s[1][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; kk++) {
+                const int i = lane >> 3;
+                const int key = warp * 16 + (i >> 1) * 8 + (lane & 7);
+                const int ch = kk * 2 + (i & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(bk + fa_off<D>(key, ch), b0, b1, b2, b3);
+                mma_bf16(s[0], qa[kk], b0, b1);
+                mma_bf16(s[1], qa[kk], b2, b3);
+            }
+            const int kbase = kt * kFaKeys + warp * 16;
+            float mx_lo = m_lo, mx_hi = m_hi;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int k0 = kbase + j * 8 + 2 * t4;
+                s[j][0] = k0 < n ? s[j][0] * sl2 : -INFINITY;
+                s[j][1] = k0 + 1 < n ? s[j][1] * sl2 : -INFINITY;
+                s[j][2] = k0 < n ? s[j][2] * sl2 : -INFINITY;
+                s[j][3] = k0 + 1 < n ? s[j][3] * sl2 : -INFINITY;
+                mx_lo = fmaxf(mx_lo, fmaxf(s[j][0], s[j][1]));
+                mx_hi = fmaxf(mx_hi, fmaxf(s[j][2], s[j][3]));
+            }
+#pragma unroll
+            for (int off = 1; off < 4; off <<= 1) {
+                mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+                mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+            }
+            const float base_lo = mx_lo == -INFINITY ? 0.f : mx_lo, base_hi = mx_hi == -INFINITY ? 0.f : mx_hi;
+            const float al_lo = exp2f(m_lo - base_lo), al_hi = exp2f(m_hi - base_hi);
+            m_lo = mx_lo; m_hi = mx_hi;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                s[j][0] = exp2f(s[j][0] - base_lo); s[j][1] = exp2f(s[j][1] - base_lo);
+                s[j][2] = exp2f(s[j][2] - base_hi); s[j][3] = exp2f(s[j][3] - base_hi);
+            }
+            l_lo = l_lo * al_lo + s[0][0] + s[0][1] + s[1][0] + s[1][1];
+            l_hi = l_hi * al_hi + s[0][2] + s[0][3] + s[1][2] + s[1][3];
+            uint32_t pa[4];
+            pa[0] = pack_bf16(s[0][0], s[0][1]);
+            pa[1] = pack_bf16(s[0][2], s[0][3]);
+            pa[2] = pack_bf16(s[1][0], s[1][1]);
+            pa[3] = pack_bf16(s[1][2], s[1][3]);
+#pragma unroll
+            for (int nj = 0; nj < D / 16; nj++) {
+                const int i = lane >> 3;
+                const int key = warp * 16 + (i & 1) * 8 + (lane & 7);
+                const int ch = nj * 2 + (i >> 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(bv + fa_off<D>(key, ch), b0, b1, b2, b3);
+                o[2 * nj][0] *= al_lo; o[2 * nj][1] *= al_lo; o[2 * nj][2] *= al_hi; o[2 * nj][3] *= al_hi;
+                o[2 * nj + 1][0] *= al_lo; o[2 * nj + 1][1] *= al_lo;
+                o[2 * nj + 1][2] *= al_hi; o[2 * nj + 1][3] *= al_hi;
+                mma_bf16(o[2 * nj], pa, b0, b1);
+                mma_bf16(o[2 * nj + 1], pa, b2, b3);
+            }
+            __syncthreads();  // stage st is refilled by a later iteration
+        }
+        cp_async_wait<0>();
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+    (void)l_hi;
+    (void)m_hi;
+
+    // ---- merge the 4 warps (rows 0..G-1 only) through shared memory ----
+    __syncthreads();
+    float *so = reinterpret_cast<float *>(fsm);  // [warp][G][D]
+    if (t4 == 0 && g < G) { wm[warp][g] = m_lo; wl[warp][g] = l_lo; }
+    if (g < G) {
+#pragma unroll
+        for (int j = 0; j < D / 8; j++) {
+            const int c = j * 8 + 2 * t4;
+            so[((size_t)warp * G + g) * D + c] = o[j][0];
+            so[((size_t)warp * G + g) * D + c + 1] = o[j][1];
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kFaWarps * 32) {
+        const int r = i / D, c = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kFaWarps; w++) M = fmaxf(M, wm[w][r]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kFaWarps; w++) {
+                const float e = exp2f(wm[w][r] - M);
+                L += wl[w][r] * e;
+                O += so[((size_t)w * G + r) * D + c] * e;
+            }
+        }
+        const int h = kvh * G + r;
+        if (a.nsplit == 1) {
+            a.out[(size_t)b * a.ld_out + (size_t)h * D + c] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+        } else {
+            const size_t pidx = ((size_t)b * H + h) * a.nsplit + split;
+            a.part_o[pidx * D + c] = O;
+            if (c == 0) { a.part_ml[pidx * 2] = M; a.part_ml[pidx * 2 + 1] = L; }
+        }
+    }
+    if (a.nsplit == 1) return;
+
+    // ---- split merge by the last CTA of this (sequence, KV head) ----
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.counters + (size_t)b * Hkv + kvh, 1u) == (unsigned)a.nsplit - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const size_t hb = (size_t)b * H + (size_t)kvh * G;
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.nsplit; sp++) M = fmaxf(M, __ldcg(a.part_ml + ((hb + tid) * a.nsplit + sp) * 2));
+        float L = 0.f;
+        for (int sp = 0; sp < a.nsplit; sp++) {
+            const float pm = __ldcg(a.part_ml + ((hb + tid) * a.nsplit + sp) * 2);
+            const float e = (M == -INFINITY || pm == -INFINITY) ? 0.f : exp2f(pm - M);
+            L += __ldcg(a.part_ml + ((hb + tid) * a.nsplit + sp) * 2 + 1) * e;
+            sw[tid][sp] = e;
+        }
+        for (int sp = 0; sp < a.nsplit; sp++) sw[tid][sp] = L > 0.f ? sw[tid][sp] / L : 0.f;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * D; i += kFaWarps * 32) {
+        const int r = i / D, c = i % D;
+        const float *po = a.part_o + (hb + r) * a.nsplit * D + c;
+        float O = 0.f;
+        for (int sp = 0; sp < a.nsplit; sp++) O += sw[r][sp] * __ldcg(po + (size_t)sp * D);
+        a.out[(size_t)b * a.ld_out + (size_t)(kvh * G + r) * D + c] = __float2bfloat16_rn(O);
+    }
+    if (tid == 0) a.counters[(size_t)b * Hkv + kvh] = 0u;
+}
+
+template <int D>
+static cudaError_t flash_decode_g(const FlashDecodeArgs &a, dim3 grid, cudaStream_t st) {
+    const size_t smem = (size_t)kFdStages * 2 * kFaKeys * D * 2;
+    switch (a.H / a.Hkv) {
+        case 1: flash_decode_kernel<D, 1><<<grid, kFaWarps * 32, smem, st>>>(a); break;
+        case 2: flash_decode_kernel<D, 2><<<grid, kFaWarps * 32, smem, st>>>(a); break;
+        case 4: flash_decode_kernel<D, 4><<<grid, kFaWarps * 32, smem, st>>>(a); break;
+        case 8: flash_decode_kernel<D, 8><<<grid, kFaWarps * 32, smem, st>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st) {
+    if (a.nsplit < 1 || a.nsplit > kFaMaxSplit) return cudaErrorInvalidValue;
+    dim3 grid(a.nsplit, a.Hkv, B);
+    if (a.d == 128) return flash_decode_g<128>(a, grid, st);
+    if (a.d == 64) return flash_decode_g<64>(a, grid, st);
+    return cudaErrorInvalidValue;
+}
+
 // ------------------------------------------------------------------------------------------
 // rows_argmax: one CTA per logits row; first index of the maximum
 // ------------------------------------------------------------------------------------------
@@ -405,7 +640,11 @@ __global__ void __launch_bounds__(512) rows_argmax_kernel(RowsArgmaxArgs a) {
 cudaError_t prefill_kernels_prepare() {
     const void *fns[] = {(const void *)norm_rows_kernel, (const void *)qkv_post_kernel<__nv_bfloat16>,
                          (const void *)qkv_post_kernel<float>, (const void *)flash_prefill_kernel<128>,
-                         (const void *)flash_prefill_kernel<64>};
+                         (const void *)flash_prefill_kernel<64>,
+                         (const void *)flash_decode_kernel<128, 1>, (const void *)flash_decode_kernel<128, 2>,
+                         (const void *)flash_decode_kernel<128, 4>, (const void *)flash_decode_kernel<128, 8>,
+                         (const void *)flash_decode_kernel<64, 1>, (const void *)flash_decode_kernel<64, 2>,
+                         (const void *)flash_decode_kernel<64, 4>, (const void *)flash_decode_kernel<64, 8>};
     for (const void *f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
         if (e != cudaSuccess) return e;

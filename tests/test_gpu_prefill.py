@@ -104,3 +104,29 @@ def test_tc_prefill_8b_layer_geometry():
         o, want = oracle_prompt_logits(c, sd, prompts[b])
         assert rel_l2(lg[b], want) < BF16_TOL
         o.close()
+
+
+@pytest.mark.parametrize("variant", [dict(), dict(head_dim=128, dim=512, heads=8, kv_heads=1)])
+def test_tc_decode_long_context_splits(variant):
+    """Five sequences prefilled to 300 positions, then batched decode: the flash-decoding attention splits
+    the context across CTAs (up to seq_len/64 splits) and merges them."""
+    c = cfg_dict(seq_len=400, **variant)
+    sd = state_dict(c, seed=29, std=0.05, norm_noise=0.1)
+    B, P = 5, 300
+    prompts = np.random.default_rng(30).integers(0, c["vocab"], (B, P)).astype(np.int32)
+    m = native_model(c, sd, precision="bf16", max_batch=B, max_tokens=B * P, page_size=32)
+    m.prefill(prompts, want_logits=False)
+    oracles = []
+    for b in range(B):
+        o = oracle_model(c, sd, bf16_weights=True)
+        for p in range(P):
+            o.forward_token(int(prompts[b, p]), p)
+        oracles.append(o)
+    nxt = np.random.default_rng(31).integers(0, c["vocab"], (3, B))
+    for step in range(3):
+        lg, _ = m.decode_step(nxt[step].tolist(), [P + step] * B)
+        for b in range(B):
+            want = oracles[b].forward_token(int(nxt[step, b]), P + step)
+            assert rel_l2(lg[b], want) < BF16_TOL, (step, b, rel_l2(lg[b], want))
+    for o in oracles:
+        o.close()
