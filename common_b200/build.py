@@ -24,6 +24,20 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", 
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 
+def _nccl_link():
+    """Link the NCCL that torch itself loads (the nvidia-nccl wheel), so that the library and torch share
+    one libnccl.so.2 in a process, whichever is loaded first; the system NCCL otherwise."""
+    try:
+        import nvidia.nccl
+        for base in nvidia.nccl.__path__:
+            lib = os.path.join(base, "lib")
+            if os.path.exists(os.path.join(lib, "libnccl.so.2")):
+                return [f"-L{lib}", "-l:libnccl.so.2", "-Xlinker", f"-rpath,{lib}"]
+    except ImportError:
+        pass
+    return ["-lnccl"]
+
+
 def _sources():
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
@@ -62,7 +76,7 @@ def build(verbose: bool = False) -> str:
             if log:
                 sys.stderr.write(log)
     if _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lnccl", "-lcudart"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + _nccl_link() + ["-lcudart"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -36,7 +36,7 @@ namespace {
 constexpr int kTcThreads = 192;
 constexpr int kBM = 128, kBK = 64;
 constexpr int kGroupT = 8;
-constexpr unsigned long long kTcWaitNs = 2000ull * 1000ull * 1000ull;  // 2 s
+constexpr unsigned long long kTcWaitNs = 4000ull * 1000ull * 1000ull;  // cycles: ~2 s at 2 GHz
 constexpr int kTcSmemBudget = 196 * 1024;
 
 __host__ __device__ constexpr int tc_stage_bytes(int bn) { return (kBM + bn) * kBK * 2; }
@@ -47,11 +47,8 @@ __host__ __device__ constexpr int tc_smem_bytes(int bn) { return tc_stages(bn) *
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ uint64_t gtime_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
+// cycle counter of this SM: cheap to read in a spin loop (the bounds below are in cycles)
+__device__ __forceinline__ uint64_t gtime_ns() { return (uint64_t)clock64(); }
 
 __device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");

@@ -118,6 +118,53 @@ cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t s
 cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st);
 cudaError_t prefill_kernels_prepare();  // opt the row kernels in to their shared memory (once, before capture)
 
+// ---- persistent batch-1 decode step (qw_step.cu) ----
+struct StepLayer {
+    const __nv_bfloat16 *w_qkv, *w_o, *w_gu, *w_down;
+    const float *b_qkv, *qn, *kn, *rms_att, *rms_ffn;
+    void *kc, *vc;  // this layer's KV pool
+};
+
+struct StepArgs {
+    const StepLayer *L;  // device array (layers)
+    int layers;
+    int D, F, V, H, Hkv, d;  // hidden, intermediate, vocab, heads, KV heads, head_dim (tp = 1)
+    const __nv_bfloat16 *embed, *lm;
+    const float *norm_final;
+    float eps, scale;
+    int qk_mode;
+    const float2 *freq;
+    const int *page_table;
+    int max_pages, page_size, log2_page;
+    const int *slots;         // device scalar (nullable: slot 0)
+    int *tokens, *positions;  // device scalars
+    int advance;
+    int *hist;
+    int *argmax_out;
+    float *logits;  // optional (V)
+    float *x, *qkv, *attn, *gu;  // work vectors (D), (Q + 2 KV), (Q), (2 F)
+    float *part_o, *part_ml;
+    unsigned *counters;  // (Hkv), zero on entry
+    float *am_val;
+    int *am_idx;
+    unsigned *am_counter;  // zero on entry
+    unsigned *bar;         // grid barrier counter, zeroed before each launch
+    float *ss;             // (layers, 2) q / k sums of squares, zeroed before each launch
+    int *err;
+    int max_k, max_rows, xs_floats;  // shared-memory layout
+    int stage_off;                   // floats: staged attention keys within the activation region
+    int kv_bf16;
+    unsigned long long *trace;       // optional: CTA 0's globaltimer before / after every grid barrier
+};
+
+size_t step_smem_bytes(const StepArgs &a);
+// Fills a.max_k / max_rows / xs_floats; false when the geometry or shared memory does not fit.
+bool step_layout(StepArgs &a, int grid, size_t *smem_out);
+cudaError_t step_prepare(bool kv_bf16, int d, int G, size_t smem);
+cudaError_t step_launch(const StepArgs &a, bool kv_bf16, int grid, cudaStream_t st);
+const void *step_kernel_fn(bool kv_bf16, int d, int G);
+constexpr int kStepBlockThreads = 288;
+
 cudaError_t gemv_launch(const GemvArgs &a, int epi, bool bf16, int num_sms, cudaStream_t st);
 cudaError_t attn_decode_launch(const AttnArgs &a, int B, bool kv_bf16, cudaStream_t st);
 

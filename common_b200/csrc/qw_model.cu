@@ -80,6 +80,13 @@ struct qw_model {
     int hist_ld = 0;
     int *h_pin_i = nullptr;  // pinned staging: tokens | positions | slots | argmax
     PrefillBuffers pf{};
+    // persistent batch-1 step kernel
+    bool use_step = false;
+    StepArgs step{};
+    StepLayer *d_step_layers = nullptr;
+    unsigned *d_bar = nullptr;
+    float *gu = nullptr;
+    unsigned long long *d_trace = nullptr;  // per-phase timestamps of a profiled step
     // graph
     cudaGraphExec_t graph = nullptr;
     int launches = 0;
@@ -382,6 +389,16 @@ qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const i
     const bool tpm = m->tp > 1;
     float *xcur = m->xa, *xalt = m->xb;
     const float *pending = nullptr;  // all-reduced partial to be added to xcur (tp > 1)
+    if (B == 1 && tokens && !x_in && m->use_step) {
+        StepArgs sa = m->step;
+        sa.tokens = next_tokens ? next_tokens : const_cast<int *>(tokens);
+        sa.positions = positions; sa.slots = slots; sa.advance = advance; sa.hist = hist;
+        sa.argmax_out = argmax_dev; sa.logits = logits_out_dev;
+        sa.trace = m->prof_on ? m->d_trace : nullptr;
+        CK(cudaMemsetAsync(sa.bar, 0, sizeof(unsigned) * (1 + 2 * (size_t)m->c.layers), m->st));
+        LKK(QW_KERNEL_STEP, step_launch(sa, m->bf16kv, m->num_sms, m->st));
+        return QW_OK;
+    }
     int nsplit = choose_nsplit(m, B);
     const void *W_embed = m->embed;
     if (x_in) {
@@ -856,6 +873,37 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
         CK(tc_prepare());
         CK(prefill_kernels_prepare());
     }
+    if (tp_size == 1 && m->bf16w && c.decode_kernels == 0) {
+        StepArgs &sa = m->step;
+        sa.layers = c.layers; sa.D = D; sa.F = m->Fl; sa.V = m->Vl; sa.H = m->Hl; sa.Hkv = m->Hkvl; sa.d = c.head_dim;
+        sa.kv_bf16 = m->bf16kv;
+        size_t smem = 0;
+        int coop = 0;
+        CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+        if (coop && step_layout(sa, m->num_sms, &smem)) {
+            CK(step_prepare(m->bf16kv, c.head_dim, m->Hl / m->Hkvl, smem));
+            int occ = 0;
+            CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel_fn(m->bf16kv, c.head_dim, m->Hl / m->Hkvl),
+                                                             kStepBlockThreads, smem));
+            if (occ >= 1) {
+                m->use_step = true;
+                sa.norm_final = m->norm_final; sa.eps = (float)c.eps; sa.scale = (float)(1.0 / sqrt((double)c.head_dim));
+                sa.qk_mode = c.qk_norm; sa.freq = m->freq; sa.page_table = m->d_page_table; sa.max_pages = m->max_pages;
+                sa.page_size = m->page_size; sa.log2_page = m->log2_page;
+                sa.x = m->xa; sa.qkv = m->qkv; sa.attn = m->attn;
+                AL(m->gu, (size_t)2 * m->Fl);
+                sa.gu = m->gu;
+                sa.part_o = m->part_o; sa.part_ml = m->part_ml; sa.counters = m->counters;
+                sa.am_val = m->am_pval; sa.am_idx = m->am_pidx; sa.am_counter = m->am_counter;
+                // barrier counter followed by the (layers, 2) sums of squares: one memset per step
+                ALB(m->d_bar, sizeof(unsigned) * (1 + 2 * (size_t)c.layers));
+                sa.bar = m->d_bar;
+                sa.ss = reinterpret_cast<float *>(m->d_bar + 1);
+                AL(m->d_trace, (size_t)2 * (5 * c.layers + 2));
+                sa.err = m->pf.d_err;
+            }
+        }
+    }
     CK(cudaStreamSynchronize(m->st));
     return QW_OK;
 }
@@ -949,6 +997,23 @@ qw_status qw_finalize_weights(qw_model *m) {
     if (c.shared_weights && !m->lm_alias)
         CK(cudaMemcpyAsync(m->lm, (char *)m->embed + (size_t)m->v0 * m->D * m->wsz, (size_t)m->Vl * m->D * m->wsz,
                            cudaMemcpyDeviceToDevice, m->st));
+    if (m->use_step && !m->d_step_layers) {
+        std::vector<StepLayer> sl(c.layers);
+        for (int l = 0; l < c.layers; l++) {
+            const Layer &Ly = m->L[l];
+            sl[l].w_qkv = (const __nv_bfloat16 *)Ly.w_qkv; sl[l].w_o = (const __nv_bfloat16 *)Ly.w_o;
+            sl[l].w_gu = (const __nv_bfloat16 *)Ly.w_gu; sl[l].w_down = (const __nv_bfloat16 *)Ly.w_down;
+            sl[l].b_qkv = Ly.b_qkv; sl[l].qn = Ly.qn; sl[l].kn = Ly.kn; sl[l].rms_att = Ly.rms_att;
+            sl[l].rms_ffn = Ly.rms_ffn;
+            sl[l].kc = (char *)m->kpool + (size_t)l * m->layer_kv_elems * m->kvsz;
+            sl[l].vc = (char *)m->vpool + (size_t)l * m->layer_kv_elems * m->kvsz;
+        }
+        AL(m->d_step_layers, c.layers);
+        CK(cudaMemcpy(m->d_step_layers, sl.data(), sizeof(StepLayer) * c.layers, cudaMemcpyHostToDevice));
+        m->step.L = m->d_step_layers;
+        m->step.lm = (const __nv_bfloat16 *)m->lm;
+        m->step.embed = (const __nv_bfloat16 *)m->embed;
+    }
     CK(cudaStreamSynchronize(m->st));
     m->finalized = true;
     return QW_OK;
@@ -1099,6 +1164,28 @@ qw_status qw_profile_decode(qw_model *m, int32_t batch, float *ms_out, int32_t *
     m->prof_on = false;
     if (s) return s;
     CK(cudaStreamSynchronize(m->st));
+    if (m->use_step && batch == 1 && m->prof_n == 1) {
+        // one persistent kernel: report its phases from CTA 0's timestamps -- the work of each
+        // phase under its kernel class, the wait in the grid barrier after it as QW_KERNEL_OTHER
+        const int nb = 5 * m->c.layers;
+        std::vector<unsigned long long> tr((size_t)2 * nb + 2);
+        CK(cudaMemcpy(tr.data(), m->d_trace, sizeof(unsigned long long) * tr.size(), cudaMemcpyDeviceToHost));
+        const int kinds[5] = {QW_KERNEL_QKV, QW_KERNEL_ATTN, QW_KERNEL_O, QW_KERNEL_GATE_UP, QW_KERNEL_DOWN};
+        int n = 0;
+        for (int i = 0; i <= nb && n + 2 <= cap; i++) {
+            ms_out[n] = (float)((double)(tr[2 * i + 1] - tr[2 * i]) * 1e-6);
+            kinds_out[n++] = i < nb ? kinds[i % 5] : QW_KERNEL_LM_HEAD;
+            if (i < nb) {
+                ms_out[n] = (float)((double)(tr[2 * i + 2] - tr[2 * i + 1]) * 1e-6);
+                kinds_out[n++] = QW_KERNEL_OTHER;
+            }
+        }
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, m->prof_ev[0], m->prof_ev[1]));
+        if (n < cap) { ms_out[n] = ms; kinds_out[n++] = QW_KERNEL_STEP; }
+        *n_out = n;
+        return QW_OK;
+    }
     for (int i = 0; i < m->prof_n; i++) {
         float ms = 0.f;
         CK(cudaEventElapsedTime(&ms, m->prof_ev[2 * i], m->prof_ev[2 * i + 1]));
@@ -1150,6 +1237,7 @@ void qw_destroy(qw_model *m) {
     cudaFree(m->part_o); cudaFree(m->part_ml); cudaFree(m->qk_ss); cudaFree(m->counters); cudaFree(m->am_counter);
     cudaFree(m->am_pval); cudaFree(m->am_pidx); cudaFree(m->am_val); cudaFree(m->am_idx); cudaFree(m->am_val_all);
     cudaFree(m->am_idx_all); cudaFree(m->logits); cudaFree(m->logits_all); cudaFree(m->d_tokens); cudaFree(m->d_argmax);
+    cudaFree(m->d_step_layers); cudaFree(m->d_bar); cudaFree(m->gu); cudaFree(m->d_trace);
     if (m->h_pin_i) cudaFreeHost(m->h_pin_i);
     prefill_free(m->pf);
     if (m->comm) ncclCommDestroy(m->comm);

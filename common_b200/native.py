@@ -26,14 +26,15 @@ EXPORTS = ("qw_abi_version", "qw_build_info", "qw_get_unique_id", "qw_create", "
            "qw_generate", "qw_decode_step_device", "qw_capture_decode", "qw_replay_decode", "qw_synchronize",
            "qw_stream", "qw_last_launch_count", "qw_last_error", "qw_destroy", "qw_profile_decode",
            "qw_set_device_inputs", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static", "qw_op_linear")
-KERNEL_NAMES = {0: "other", 1: "qkv", 2: "attn", 3: "o_proj", 4: "gate_up", 5: "down", 6: "lm_head"}
+KERNEL_NAMES = {0: "other", 1: "qkv", 2: "attn", 3: "o_proj", 4: "gate_up", 5: "down", 6: "lm_head", 7: "step"}
 
 
 class QwConfig(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "dim", "hidden_dim", "layers", "heads", "kv_heads", "head_dim", "vocab", "seq_len", "shared_weights",
-        "qk_norm", "has_qkv_bias", "weight_dtype", "kv_dtype", "max_batch", "max_tokens", "page_size", "num_pages")] + \
-        [("reserved", C.c_int32 * 5), ("rope_theta", C.c_double), ("eps", C.c_double)]
+        "qk_norm", "has_qkv_bias", "weight_dtype", "kv_dtype", "max_batch", "max_tokens", "page_size", "num_pages",
+        "decode_kernels")] + \
+        [("reserved", C.c_int32 * 4), ("rope_theta", C.c_double), ("eps", C.c_double)]
 
 
 class QwenError(RuntimeError):
@@ -103,12 +104,14 @@ def _fp(a):
 
 def make_config(dim, hidden_dim, layers, heads, kv_heads, head_dim, vocab, seq_len, shared_weights=False,
                 qk_norm=QKNORM_VECTOR, has_qkv_bias=False, weight_dtype=DTYPE_BF16, kv_dtype=DTYPE_BF16,
-                max_batch=1, max_tokens=0, page_size=64, num_pages=0, rope_theta=1e6, eps=1e-6) -> QwConfig:
+                max_batch=1, max_tokens=0, page_size=64, num_pages=0, rope_theta=1e6, eps=1e-6,
+                decode_kernels=0) -> QwConfig:
     c = QwConfig()
     c.dim, c.hidden_dim, c.layers, c.heads, c.kv_heads, c.head_dim = dim, hidden_dim, layers, heads, kv_heads, head_dim
     c.vocab, c.seq_len, c.shared_weights, c.qk_norm, c.has_qkv_bias = vocab, seq_len, int(shared_weights), qk_norm, int(has_qkv_bias)
     c.weight_dtype, c.kv_dtype, c.max_batch, c.max_tokens = weight_dtype, kv_dtype, max_batch, max_tokens or max_batch
     c.page_size, c.num_pages, c.rope_theta, c.eps = page_size, num_pages, rope_theta, eps
+    c.decode_kernels = decode_kernels
     return c
 
 

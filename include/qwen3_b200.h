@@ -76,7 +76,9 @@ typedef struct qw_config {
     int32_t max_tokens;     /* max tokens in one prefill call (activation arena), >= max_batch */
     int32_t page_size;      /* KV page size in tokens (power of two, 16..256); 0 = 64 */
     int32_t num_pages;      /* KV pages per rank; 0 = max_batch * ceil(seq_len / page_size) */
-    int32_t reserved[5];
+    int32_t decode_kernels; /* batch-1 decode at tp 1 with bf16 weights: 0 = one persistent kernel per step
+                               (auto), 1 = one kernel per operation */
+    int32_t reserved[4];
     double rope_theta;      /* 1e6 for Qwen3 */
     double eps;             /* rmsnorm epsilon, 1e-6 for Qwen3 */
 } qw_config;
@@ -174,7 +176,8 @@ enum {
     QW_KERNEL_O = 3,       /* o projection + residual */
     QW_KERNEL_GATE_UP = 4, /* rmsnorm + gate/up projection + SwiGLU */
     QW_KERNEL_DOWN = 5,    /* down projection + residual */
-    QW_KERNEL_LM_HEAD = 6  /* final rmsnorm + lm_head + argmax */
+    QW_KERNEL_LM_HEAD = 6, /* final rmsnorm + lm_head + argmax */
+    QW_KERNEL_STEP = 7     /* the whole batch-1 decode step in one persistent kernel */
 };
 
 /* Set the device-side token / position of sequences 0..batch-1 (slots 0..batch-1) used by

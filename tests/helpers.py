@@ -51,12 +51,12 @@ def state_dict(c, seed=0, std=0.02, norm_noise=0.0):
 
 
 def native_model(c, sd=None, precision="fp32", kv=None, max_batch=1, max_tokens=0, page_size=64, num_pages=0,
-                 synthetic_seed=None, device=0):
+                 synthetic_seed=None, device=0, decode_kernels=0):
     dt = {"fp32": native.DTYPE_F32, "bf16": native.DTYPE_BF16}
     cfg = native.make_config(c["dim"], c["hidden_dim"], c["layers"], c["heads"], c["kv_heads"], c["head_dim"],
                              c["vocab"], c["seq_len"], c["shared_weights"], c["qk_norm"], c["has_qkv_bias"],
                              dt[precision], dt[kv or precision], max_batch, max_tokens, page_size, num_pages,
-                             c["rope_theta"], c["eps"])
+                             c["rope_theta"], c["eps"], decode_kernels)
     m = native.NativeModel(cfg, device)
     if sd is not None:
         for k, v in sd.items():
