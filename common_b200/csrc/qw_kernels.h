@@ -144,7 +144,7 @@ struct StepArgs {
     float *logits;  // optional (V)
     float *x, *qkv, *attn, *gu;  // work vectors (D), (Q + 2 KV), (Q), (2 F)
     float *part_o, *part_ml;
-    unsigned *counters;  // (Hkv), zero on entry
+    unsigned *counters;  // (layers, Hkv) attention split arrivals, zeroed before each launch
     float *am_val;
     int *am_idx;
     unsigned *am_counter;  // zero on entry

@@ -85,6 +85,7 @@ struct qw_model {
     StepArgs step{};
     StepLayer *d_step_layers = nullptr;
     unsigned *d_bar = nullptr;
+    size_t step_zero_words = 0;
     float *gu = nullptr;
     unsigned long long *d_trace = nullptr;  // per-phase timestamps of a profiled step
     // graph
@@ -395,7 +396,7 @@ qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const i
         sa.positions = positions; sa.slots = slots; sa.advance = advance; sa.hist = hist;
         sa.argmax_out = argmax_dev; sa.logits = logits_out_dev;
         sa.trace = m->prof_on ? m->d_trace : nullptr;
-        CK(cudaMemsetAsync(sa.bar, 0, sizeof(unsigned) * (1 + 2 * (size_t)m->c.layers), m->st));
+        CK(cudaMemsetAsync(sa.bar, 0, sizeof(unsigned) * m->step_zero_words, m->st));
         LKK(QW_KERNEL_STEP, step_launch(sa, m->bf16kv, m->num_sms, m->st));
         return QW_OK;
     }
@@ -893,12 +894,15 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 sa.x = m->xa; sa.qkv = m->qkv; sa.attn = m->attn;
                 AL(m->gu, (size_t)2 * m->Fl);
                 sa.gu = m->gu;
-                sa.part_o = m->part_o; sa.part_ml = m->part_ml; sa.counters = m->counters;
+                sa.part_o = m->part_o; sa.part_ml = m->part_ml;
                 sa.am_val = m->am_pval; sa.am_idx = m->am_pidx; sa.am_counter = m->am_counter;
-                // barrier counter followed by the (layers, 2) sums of squares: one memset per step
-                ALB(m->d_bar, sizeof(unsigned) * (1 + 2 * (size_t)c.layers));
+                // per-step state, zeroed by one memset before every launch: barrier counter,
+                // (layers, 2) q/k sums of squares, (layers, Hkv) attention split arrivals
+                m->step_zero_words = 1 + 2 * (size_t)c.layers + (size_t)c.layers * m->Hkvl;
+                ALB(m->d_bar, sizeof(unsigned) * m->step_zero_words);
                 sa.bar = m->d_bar;
                 sa.ss = reinterpret_cast<float *>(m->d_bar + 1);
+                sa.counters = m->d_bar + 1 + 2 * c.layers;
                 AL(m->d_trace, (size_t)2 * (5 * c.layers + 2));
                 sa.err = m->pf.d_err;
             }

@@ -42,7 +42,7 @@ constexpr int kRows = 4;        // weight rows per ring slot
 constexpr int kPiece = 32768;  // bytes per ring slot (kRows rows x up to 4096 columns)
 constexpr int kRing = 5;
 constexpr unsigned long long kStepWaitNs = 4000ull * 1000ull * 1000ull;  // cycles: ~2 s at 2 GHz
-constexpr int kStepTPW = 8;  // attention: keys per warp per tile
+constexpr int kStepTPW = 4;  // attention: keys per warp per tile (small: this code runs once per layer, cold in the instruction cache)
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 // cycle counter of this SM: cheap to read in a spin loop (the bounds below are in cycles)
@@ -401,7 +401,6 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     float *wl = wm + 8 * G;         // [8][G]
     float *mlm = wl + 8 * G;        // [G][64] split maxima, then weights
     float *mll = mlm + G * 64;      // [G][64] split sums
-    int *s_last = reinterpret_cast<int *>(mll + G * 64);
     const int pos = *a.positions;
     const int n = pos + 1;
     const int chunk = (n + ns - 1) / ns;
@@ -630,50 +629,71 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         }
     }
     if (ns == 1) return;
-    // ---- the last CTA of this KV head merges the splits (all loads issued in parallel) ----
+    // ---- every split CTA of this KV head waits for all partials, then merges its slice of the output ----
     __threadfence();
     consumers_sync();
-    if (tid == 0) *s_last = atomicAdd(a.counters + kvh, 1u) == (unsigned)ns - 1;
+    unsigned *cnt = a.counters + (size_t)layer * a.Hkv + kvh;  // zeroed before the launch
+    if (tid == 0) {
+        atomicAdd(cnt, 1u);
+        const uint64_t w0 = now_ns();
+        while (ld_acquire(cnt) < (unsigned)ns) {
+            if (now_ns() - w0 > kStepWaitNs) { atomicExch(a.err, 3); break; }
+        }
+        __threadfence();
+    }
     consumers_sync();
-    if (!*s_last) return;
-    __threadfence();
-    for (int i = tid; i < G * ns; i += kStepConsumers) {
-        const int g = i / ns, sidx = i % ns;
+    const int per = (G * D + ns - 1) / ns;
+    const int i0 = sp * per, i1 = min(G * D, i0 + per);
+    // the (max, sum) of every split of the heads this slice touches, and the slice's partial outputs,
+    // loaded in one batch
+    const int g0 = i0 / D, g1 = (i1 - 1) / D;
+    for (int i = tid; i < (g1 - g0 + 1) * ns; i += kStepConsumers) {
+        const int g = g0 + i / ns, sidx = i % ns;
         const float2 ml = __ldcg(reinterpret_cast<const float2 *>(a.part_ml) + (size_t)(kvh * G + g) * ns + sidx);
         mlm[g * 64 + sidx] = ml.x;
         mll[g * 64 + sidx] = ml.y;
     }
+    constexpr int kMaxPV = 24;
+    float pv[kMaxPV];
+    const int oi = i0 + tid;  // one output per thread (per <= 256 whenever ns >= 2 for G*D <= 512)
+    const bool mine = oi < i1 && ns <= kMaxPV;
+    if (mine) {
+        const float *po = a.part_o + (size_t)(kvh * G + oi / D) * ns * D + oi % D;
+#pragma unroll
+        for (int sidx = 0; sidx < kMaxPV; sidx++) pv[sidx] = sidx < ns ? __ldcg(po + (size_t)sidx * D) : 0.f;
+    }
     consumers_sync();
-    if (tid < G) {
+    if (tid <= g1 - g0) {
+        const int g = g0 + tid;
         float M = -INFINITY;
-        for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[tid * 64 + sidx]);
+        for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[g * 64 + sidx]);
         float L = 0.f;
         for (int sidx = 0; sidx < ns; sidx++) {
-            const float pm = mlm[tid * 64 + sidx];
+            const float pm = mlm[g * 64 + sidx];
             const float e = pm == -INFINITY ? 0.f : expf(pm - M);
-            L += mll[tid * 64 + sidx] * e;
-            mlm[tid * 64 + sidx] = e;
+            L += mll[g * 64 + sidx] * e;
+            mlm[g * 64 + sidx] = e;
         }
         const float inv = 1.0f / L;
-        for (int sidx = 0; sidx < ns; sidx++) mlm[tid * 64 + sidx] *= inv;
+        for (int sidx = 0; sidx < ns; sidx++) mlm[g * 64 + sidx] *= inv;
     }
     consumers_sync();
-    for (int i = tid; i < G * D; i += kStepConsumers) {
-        const int g = i / D, j = i % D;
-        const float *po = a.part_o + (size_t)(kvh * G + g) * ns * D + j;
+    if (mine) {
+        const int g = oi / D;
         float O = 0.f;
-        int sidx = 0;
-        for (; sidx + 8 <= ns; sidx += 8) {
-            float pv[8];
 #pragma unroll
-            for (int u = 0; u < 8; u++) pv[u] = __ldcg(po + (size_t)(sidx + u) * D);
-#pragma unroll
-            for (int u = 0; u < 8; u++) O += mlm[g * 64 + sidx + u] * pv[u];
+        for (int sidx = 0; sidx < kMaxPV; sidx++)
+            if (sidx < ns) O += mlm[g * 64 + sidx] * pv[sidx];
+        a.attn[(size_t)kvh * G * D + oi] = O;
+    } else if (ns > kMaxPV) {
+        for (int o = i0 + tid; o < i1; o += kStepConsumers) {
+            const int g = o / D;
+            const float *po = a.part_o + (size_t)(kvh * G + g) * ns * D + o % D;
+            float O = 0.f;
+            for (int sidx = 0; sidx < ns; sidx++) O += mlm[g * 64 + sidx] * __ldcg(po + (size_t)sidx * D);
+            a.attn[(size_t)kvh * G * D + o] = O;
         }
-        for (; sidx < ns; sidx++) O += mlm[g * 64 + sidx] * __ldcg(po + (size_t)sidx * D);
-        a.attn[(size_t)(kvh * G + g) * D + j] = O;
     }
-    if (tid == 0) a.counters[kvh] = 0u;
 }
 
 template <typename KT, int D, int G>
