@@ -249,11 +249,8 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     build.build()
-    nid = None
-    if world > 1:
-        obj = [native.unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nid = obj[0]
+    from common_b200 import parallel
+    nid = parallel.share_unique_id(native.unique_id)  # one NCCL id per communicator (per model)
     g = GEOM_8B
     B = 1
     e2e_steps = args.e2e_steps
@@ -359,7 +356,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     batched = None
     if not args.no_batched:
-        batched = run_batched(args, rank, world, local, nid, peaks)
+        batched = run_batched(args, rank, world, local, parallel.share_unique_id(native.unique_id), peaks)
         torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
