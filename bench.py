@@ -279,6 +279,7 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     m.replay_decode(args.warmup)
+    m.synchronize()  # raises if a bounded device-side wait gave up
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
@@ -289,6 +290,7 @@ def run_ours(args):
     m.replay_decode(args.steps)
     e1.record(stream)
     barrier()
+    m.synchronize()
     ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     if world > 1:

@@ -43,7 +43,7 @@ __host__ __device__ constexpr int tc_stage_bytes(int bn) { return (kBM + bn) * k
 __host__ __device__ constexpr int tc_stages(int bn) {
     return kTcSmemBudget / tc_stage_bytes(bn) > 8 ? 8 : kTcSmemBudget / tc_stage_bytes(bn);
 }
-__host__ __device__ constexpr int tc_smem_bytes(int bn) { return tc_stages(bn) * tc_stage_bytes(bn) + 1024; }
+__host__ __device__ constexpr int tc_smem_bytes(int bn) { return tc_stages(bn) * tc_stage_bytes(bn) + 1024 + 4096; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = smem;
     uint8_t *sB = smem + S * A_BYTES;
+    uint8_t *sStage = smem + S * (A_BYTES + B_BYTES);  // SWIGLU epilogue: [32 tokens][64 pairs] bf16
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int *abort_flag = &abort_sh;
 
@@ -286,17 +287,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + cc), r);
                 const int nj = min(32, ncols - cc);
                 if (EPI == TC_SWIGLU) {
-                    __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(a.out);
-                    const int pair = ((c.f0 + q * 32) >> 1) + lane;
+                    // up * silu(gate) for this warp's 16 pairs x 32 tokens, staged as [token][64 pairs] bf16
+                    // so that the 4 epilogue warps then write whole 128-byte rows
+                    uint16_t *stg = reinterpret_cast<uint16_t *>(sStage);
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const float g = __uint_as_float(r[j]);
                         const float u = __shfl_down_sync(0xffffffffu, g, 16);
-                        if (lane < 16 && j < nj && c.f0 + q * 32 < a.M) {
-                            const float sg = 1.0f / (1.0f + expf(-g));
-                            o[(size_t)(tbase + cc + j) * a.ld_out + pair] = __float2bfloat16_rn(u * (g * sg));
+                        if (lane < 16) {
+                            const float h = u * __fdividef(g, 1.0f + __expf(-g));
+                            stg[j * 64 + q * 16 + lane] = f2bf_bits(h);
                         }
                     }
+                    asm volatile("bar.sync 2, 128;" ::: "memory");
+                    {
+                        const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
+                        const int pair0 = c.f0 >> 1;
+                        const int npair = min(64, (a.M - c.f0) >> 1);
+                        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(a.out);
+#pragma unroll
+                        for (int k2 = 0; k2 < 2; k2++) {
+                            const int idx = et + k2 * 128;  // 256 chunks of 16 bytes: 32 rows x 8
+                            const int row = idx >> 3, ch = idx & 7;
+                            if (row < nj && ch * 8 < npair) {
+                                const uint4 v = *reinterpret_cast<const uint4 *>(stg + row * 64 + ch * 8);
+                                *reinterpret_cast<uint4 *>(o + (size_t)(tbase + cc + row) * a.ld_out + pair0 + ch * 8) = v;
+                            }
+                        }
+                    }
+                    asm volatile("bar.sync 2, 128;" ::: "memory");
                 } else if (f < a.M) {
                     float *o = reinterpret_cast<float *>(a.out);
                     const float bias = (a.bias && c.ks == 0) ? a.bias[f] : 0.f;

@@ -145,12 +145,18 @@ struct StepArgs {
     float *x, *qkv, *attn, *gu;  // work vectors (D), (Q + 2 KV), (Q), (2 F)
     float *part_o, *part_ml;
     unsigned *counters;  // (layers, Hkv) attention split arrivals, zeroed before each launch
-    float *am_val;
+    float *am_val;         // (grid) per-CTA argmax candidates
     int *am_idx;
-    unsigned *am_counter;  // zero on entry
     unsigned *bar;         // grid barrier counter, zeroed before each launch
     float *ss;             // (layers, 2) q / k sums of squares, zeroed before each launch
     int *err;
+    // tensor parallelism (tp = 1: none)
+    int tp, rank, v0;          // ranks, this rank, first vocabulary row of this rank's lm_head shard
+    int q_total, kv_total;     // global q / k widths (whole-vector QK-norm denominators)
+    float *x2;                 // second residual-stream buffer (tp > 1)
+    unsigned *const *xch;      // device array [tp]: every rank's exchange buffer (peer pointers)
+    unsigned *gen;             // cross-rank barriers passed, persistent across steps
+    unsigned *layers_done;     // layers run by earlier steps, persistent
     int max_k, max_rows, xs_floats;  // shared-memory layout
     int stage_off;                   // floats: staged attention keys within the activation region
     int kv_bf16;

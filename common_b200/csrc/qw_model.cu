@@ -88,6 +88,10 @@ struct qw_model {
     size_t step_zero_words = 0;
     float *gu = nullptr;
     unsigned long long *d_trace = nullptr;  // per-phase timestamps of a profiled step
+    unsigned *xch = nullptr;                // this rank's exchange buffer (tensor parallel step kernel)
+    std::vector<void *> xch_peer;           // peers' exchange buffers opened through CUDA IPC
+    unsigned **d_xch = nullptr;             // device array of all ranks' exchange buffers
+    unsigned *d_persist = nullptr;          // barrier generation + release word, persistent
     // graph
     cudaGraphExec_t graph = nullptr;
     int launches = 0;
@@ -390,7 +394,7 @@ qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const i
     const bool tpm = m->tp > 1;
     float *xcur = m->xa, *xalt = m->xb;
     const float *pending = nullptr;  // all-reduced partial to be added to xcur (tp > 1)
-    if (B == 1 && tokens && !x_in && m->use_step) {
+    if (B == 1 && tokens && !x_in && m->use_step && (m->tp == 1 || !logits_out_dev)) {
         StepArgs sa = m->step;
         sa.tokens = next_tokens ? next_tokens : const_cast<int *>(tokens);
         sa.positions = positions; sa.slots = slots; sa.advance = advance; sa.hist = hist;
@@ -759,6 +763,39 @@ qw_status qw_get_unique_id(void *out128) {
     return QW_OK;
 }
 
+// Exchange buffers of the tensor-parallel step kernel: every rank allocates one, shares its CUDA IPC
+// handle through an NCCL all-gather and opens the others' (peer access over NVLink).
+static qw_status setup_exchange(qw_model *m) {
+    const int tp = m->tp;
+    const size_t words = 128 + (size_t)2 * tp * m->D;
+    CK(cudaMalloc((void **)&m->xch, words * sizeof(unsigned)));
+    CK(cudaMemset(m->xch, 0, words * sizeof(unsigned)));
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, m->xch));
+    char *d_h = nullptr;
+    CK(cudaMalloc((void **)&d_h, sizeof(h) * (tp + 1)));
+    CK(cudaMemcpy(d_h + sizeof(h) * tp, &h, sizeof(h), cudaMemcpyHostToDevice));
+    ncclResult_t nr = ncclAllGather(d_h + sizeof(h) * tp, d_h, sizeof(h), ncclChar, m->comm, m->st);
+    std::vector<cudaIpcMemHandle_t> all(tp);
+    cudaError_t e = cudaStreamSynchronize(m->st);
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), d_h, sizeof(h) * tp, cudaMemcpyDeviceToHost);
+    cudaFree(d_h);
+    if (nr != ncclSuccess) return fail(m, QW_ERR_NCCL, "exchange handles: %s", ncclGetErrorString(nr));
+    if (e != cudaSuccess) return fail(m, QW_ERR_CUDA, "exchange handles: %s", cudaGetErrorString(e));
+    std::vector<unsigned *> ptrs(tp);
+    m->xch_peer.assign(tp, nullptr);
+    for (int p = 0; p < tp; p++) {
+        if (p == m->rank) { ptrs[p] = m->xch; continue; }
+        void *q = nullptr;
+        CK(cudaIpcOpenMemHandle(&q, all[p], cudaIpcMemLazyEnablePeerAccess));
+        m->xch_peer[p] = q;
+        ptrs[p] = (unsigned *)q;
+    }
+    AL(m->d_xch, tp);
+    CK(cudaMemcpy(m->d_xch, ptrs.data(), sizeof(unsigned *) * tp, cudaMemcpyHostToDevice));
+    return QW_OK;
+}
+
 static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int tp_rank, int tp_size,
                              const void *nccl_id) {
     const qw_config &c = *cfg;
@@ -874,7 +911,7 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
         CK(tc_prepare());
         CK(prefill_kernels_prepare());
     }
-    if (tp_size == 1 && m->bf16w && c.decode_kernels == 0) {
+    if (m->bf16w && c.decode_kernels == 0) {
         StepArgs &sa = m->step;
         sa.layers = c.layers; sa.D = D; sa.F = m->Fl; sa.V = m->Vl; sa.H = m->Hl; sa.Hkv = m->Hkvl; sa.d = c.head_dim;
         sa.kv_bf16 = m->bf16kv;
@@ -895,7 +932,7 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 AL(m->gu, (size_t)2 * m->Fl);
                 sa.gu = m->gu;
                 sa.part_o = m->part_o; sa.part_ml = m->part_ml;
-                sa.am_val = m->am_pval; sa.am_idx = m->am_pidx; sa.am_counter = m->am_counter;
+                sa.am_val = m->am_pval; sa.am_idx = m->am_pidx;
                 // per-step state, zeroed by one memset before every launch: barrier counter,
                 // (layers, 2) q/k sums of squares, (layers, Hkv) attention split arrivals
                 m->step_zero_words = 1 + 2 * (size_t)c.layers + (size_t)c.layers * m->Hkvl;
@@ -905,6 +942,18 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 sa.counters = m->d_bar + 1 + 2 * c.layers;
                 AL(m->d_trace, (size_t)2 * (5 * c.layers + 2));
                 sa.err = m->pf.d_err;
+                sa.tp = tp_size; sa.rank = tp_rank; sa.v0 = m->v0;
+                sa.q_total = c.heads * c.head_dim; sa.kv_total = c.kv_heads * c.head_dim;
+                sa.x2 = m->xb;
+                AL(m->d_persist, 2);
+                CK(cudaMemset(m->d_persist, 0, 2 * sizeof(unsigned)));
+                sa.gen = m->d_persist;
+                sa.layers_done = m->d_persist + 1;
+                if (tp_size > 1) {
+                    qw_status st = setup_exchange(m);
+                    if (st) return st;
+                    sa.xch = m->d_xch;
+                }
             }
         }
     }
@@ -1215,6 +1264,11 @@ qw_status qw_synchronize(qw_model *m) {
     if (!m) return QW_ERR_ARG;
     CK(cudaSetDevice(m->dev));
     CK(cudaStreamSynchronize(m->st));
+    // a bounded wait inside a kernel that gave up records its site in the device error word:
+    // 1 weight slot, 2 grid barrier, 3 attention split merge, 4 cross-rank barrier, 5 final argmax exchange
+    int derr = 0;
+    CK(cudaMemcpy(&derr, m->pf.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (derr) return fail(m, QW_ERR_TIMEOUT, "a device-side wait gave up (site %d)", derr);
     return QW_OK;
 }
 
@@ -1242,6 +1296,9 @@ void qw_destroy(qw_model *m) {
     cudaFree(m->am_pval); cudaFree(m->am_pidx); cudaFree(m->am_val); cudaFree(m->am_idx); cudaFree(m->am_val_all);
     cudaFree(m->am_idx_all); cudaFree(m->logits); cudaFree(m->logits_all); cudaFree(m->d_tokens); cudaFree(m->d_argmax);
     cudaFree(m->d_step_layers); cudaFree(m->d_bar); cudaFree(m->gu); cudaFree(m->d_trace);
+    for (void *q : m->xch_peer)
+        if (q) cudaIpcCloseMemHandle(q);
+    cudaFree(m->xch); cudaFree(m->d_xch); cudaFree(m->d_persist);
     if (m->h_pin_i) cudaFreeHost(m->h_pin_i);
     prefill_free(m->pf);
     if (m->comm) ncclCommDestroy(m->comm);

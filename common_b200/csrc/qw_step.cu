@@ -42,6 +42,11 @@ constexpr int kRows = 4;        // weight rows per ring slot
 constexpr int kPiece = 32768;  // bytes per ring slot (kRows rows x up to 4096 columns)
 constexpr int kRing = 5;
 constexpr unsigned long long kStepWaitNs = 4000ull * 1000ull * 1000ull;  // cycles: ~2 s at 2 GHz
+// layout of a rank's exchange buffer (32-bit words): flags, QK-norm sums, argmax, row partials
+constexpr int kXFlags = 0;   // [tp] generation flags, written by each peer
+constexpr int kXSs = 64;     // [2][2] q / k sums of squares accumulated over all ranks (even / odd layers)
+constexpr int kXAm = 96;     // [tp][2] (value, index) of each rank's vocabulary shard
+constexpr int kXRows = 128;  // [2][tp][D]: O partials, then down partials
 constexpr int kStepTPW = 4;  // attention: keys per warp per tile (small: this code runs once per layer, cold in the instruction cache)
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -107,7 +112,9 @@ struct Ring {
 
 // Column chunk of one ring slot: a slot holds the same C columns of kRows consecutive rows, so every
 // activation value read from shared memory serves kRows weight rows.
-__device__ __forceinline__ int chunk_cols(int K) { return (K & 4095) == 0 ? 4096 : ((K & 2047) == 0 ? 2048 : 1024); }
+__host__ __device__ __forceinline__ int chunk_cols(int K) {
+    return (K & 4095) == 0 ? 4096 : ((K & 2047) == 0 ? 2048 : ((K & 1023) == 0 ? 1024 : 512));
+}
 
 // producer: this CTA's rows [r0, r1) of W (N, K), kRows rows at a time, each group in column chunks
 __device__ __forceinline__ bool produce(Ring &rg, const __nv_bfloat16 *W, int N, int K, volatile int *abort_flag,
@@ -171,6 +178,7 @@ __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, floa
                                           volatile int *abort_flag, int *err) {
     constexpr int PER_WARP = C / 8;
     constexpr int STEPS = PER_WARP / 128;
+    static_assert(STEPS >= 1, "C >= 1024 (see consume_512)");
     static_assert(kRows == 4, "warp_sum4 reduces four rows");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cw = warp * PER_WARP + lane * 4;
@@ -216,6 +224,36 @@ __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, floa
     return true;
 }
 
+// C = 512 (K an odd multiple of 512, e.g. a tensor-parallel shard): warp w takes 64 columns of each
+// slot, lane l columns 2l, 2l+1
+__device__ __forceinline__ bool consume_512(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+                                            volatile int *abort_flag, int *err) {
+    constexpr int C = 512;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cw = warp * 64 + lane * 2;
+    for (int ra = r0; ra < r1; ra += kRows) {
+        const int nr = min(kRows, r1 - ra);
+        float p[kRows] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err)) return false;
+            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
+            const float2 x = *reinterpret_cast<const float2 *>(xs + c0 + cw);
+            uint32_t w[kRows];
+#pragma unroll
+            for (int r = 0; r < kRows; r++) w[r] = *reinterpret_cast<const uint32_t *>(sa + (size_t)r * C * 2);
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+#pragma unroll
+            for (int r = 0; r < kRows; r++) p[r] = fmaf(bf16hi(w[r]), x.y, fmaf(bf16lo(w[r]), x.x, p[r]));
+        }
+        const float tot = warp_sum4(p[0], p[1], p[2], p[3]);
+        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
+    }
+    return true;
+}
+
 __device__ __forceinline__ bool consume(Ring &rg, int N, int K, const float *xs, float *acc, int &r0, int &r1,
                                         volatile int *abort_flag, int *err) {
     split_rows(N, blockIdx.x, gridDim.x, r0, r1);
@@ -226,7 +264,8 @@ __device__ __forceinline__ bool consume(Ring &rg, int N, int K, const float *xs,
     switch (chunk_cols(K)) {
         case 4096: ok = consume_c<4096>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
         case 2048: ok = consume_c<2048>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
-        default: ok = consume_c<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 1024: ok = consume_c<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        default: ok = consume_512(rg, K, xs, acc, r0, r1, abort_flag, err); break;
     }
     if (!ok) return false;
     consumers_sync();
@@ -257,6 +296,109 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned &target, volat
     }
     consumers_sync();
     return !*abort_flag;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_release_sys(unsigned *p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// What every CTA adds to every rank's exchange buffer before arriving at a cross-rank barrier.
+enum { PUB_NONE = 0, PUB_SS = 1 };
+
+// Barrier over every CTA of every tensor-parallel rank, flat: each CTA fences its stores (including
+// the NVLink stores into the peers' inboxes) at system scope and adds one, with release semantics, to
+// its rank's arrival counter in every rank's exchange buffer; then every CTA waits until the counters
+// in its own GPU's buffer show all CTAs of all ranks.  Counters grow monotonically across barriers
+// and steps (gen = barriers passed so far), compared with wrap-around arithmetic.  PUB_SS also adds
+// this CTA's q / k sums of squares into every rank's per-layer accumulator.
+__device__ __forceinline__ bool cross_sync(const StepArgs &a, unsigned &target, unsigned &gen, int pub, int layer,
+                                           float sq, float sk, volatile int *abort_flag) {
+    consumers_sync();
+    const unsigned idx = target / gridDim.x;
+    target += gridDim.x;
+    gen += 1u;
+    if (threadIdx.x == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 1] = trace_ns();
+    if (threadIdx.x == 0) {
+        atomicAdd(a.bar, 1u);  // keeps the local barrier counter in step with `target`
+        if (pub == PUB_SS)
+            for (int p = 0; p < a.tp; p++) {
+                float *acc2 = reinterpret_cast<float *>(a.xch[p]) + kXSs + 2 * (layer & 1);  // layer: global count
+                atomicAdd(acc2, sq);
+                atomicAdd(acc2 + 1, sk);
+            }
+        __threadfence_system();
+        for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, 1u);
+        const unsigned want = gen * gridDim.x;
+        const unsigned *mine = a.xch[a.rank] + kXFlags;
+        const uint64_t t0 = now_ns();
+        bool ok = true;
+        for (int p = 0; ok && p < a.tp; p++)
+            while ((int)(ld_acquire_sys(mine + p) - want) < 0)
+                if (*abort_flag || now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+        if (!ok) {
+            *abort_flag = 1;
+            atomicExch(a.err, 4);
+        }
+        if (a.trace && blockIdx.x == 0) a.trace[2 * idx + 2] = trace_ns();
+    }
+    consumers_sync();
+    return !*abort_flag;
+}
+
+// this rank's partial of rows [r0, r1) of a row-split projection into inbox slot `rank` of every rank
+__device__ __forceinline__ void push_partial(const StepArgs &a, int box, int r0, int r1, const float *acc) {
+    for (int r = threadIdx.x; r < r1 - r0; r += kStepConsumers) {
+        const float v = acc[r];
+        for (int p = 0; p < a.tp; p++)
+            reinterpret_cast<float *>(a.xch[p])[box + (size_t)a.rank * a.D + r0 + r] = v;
+    }
+}
+
+// xs = rmsnorm(x + sum over ranks of the inbox partials) * w; the rows this CTA owns of the
+// un-normalised sum are written to xnext (the residual stream's other buffer)
+__device__ __forceinline__ void load_resid(const StepArgs &a, float *xs, const float *xcur, int box, float *xnext,
+                                           const float *w, float *red) {
+    const int tid = threadIdx.x, K = a.D;
+    const float *in = reinterpret_cast<const float *>(a.xch[a.rank]) + box;
+    int o0, o1;
+    split_rows(K, blockIdx.x, gridDim.x, o0, o1);
+    float ss = 0.f;
+    for (int q = tid; q < (K >> 2); q += kStepConsumers) {
+        float4 v = __ldcg(reinterpret_cast<const float4 *>(xcur) + q);
+        for (int p = 0; p < a.tp; p++) {
+            const float4 t = __ldcg(reinterpret_cast<const float4 *>(in + (size_t)p * K) + q);
+            v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+        }
+        reinterpret_cast<float4 *>(xs)[q] = v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    consumers_sync();
+    for (int k = o0 + tid; k < o1; k += kStepConsumers) xnext[k] = xs[k];
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kStepConsumerWarps; i++) tot += red[i];
+    const float sc = 1.0f / sqrtf(tot / (float)K + a.eps);
+    for (int q = tid; q < (K >> 2); q += kStepConsumers) {
+        float4 v = reinterpret_cast<float4 *>(xs)[q];
+        const float4 g = reinterpret_cast<const float4 *>(w)[q];
+        v.x = g.x * v.x * sc; v.y = g.y * v.y * sc; v.z = g.z * v.z * sc; v.w = g.w * v.w * sc;
+        reinterpret_cast<float4 *>(xs)[q] = v;
+    }
+    consumers_sync();
 }
 
 // xs = rmsnorm(src) * w over K elements (src read through L2); with w == nullptr a plain copy.
@@ -409,8 +551,17 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     // ---- q heads, k, v of this KV head (one float4 per thread for d 128, G 4) ----
     float scq = 1.f, sck = 1.f;
     if (a.qk_mode == 1) {
-        scq = 1.0f / sqrtf(__ldcg(a.ss + 2 * layer) / (float)Q + 1e-6f);
-        sck = 1.0f / sqrtf(__ldcg(a.ss + 2 * layer + 1) / (float)KVw + 1e-6f);
+        float tq = 0.f, tk = 0.f;
+        if (a.tp > 1) {  // every CTA of every rank added its sums into this rank's accumulator
+            const float *in = reinterpret_cast<const float *>(a.xch[a.rank]) + kXSs + 2 * ((*a.layers_done + layer) & 1);
+            tq = __ldcg(in);
+            tk = __ldcg(in + 1);
+        } else {
+            tq = __ldcg(a.ss + 2 * layer);
+            tk = __ldcg(a.ss + 2 * layer + 1);
+        }
+        scq = 1.0f / sqrtf(tq / (float)a.q_total + 1e-6f);
+        sck = 1.0f / sqrtf(tk / (float)a.kv_total + 1e-6f);
     }
     constexpr int NQ4 = G * D / 4, NK4 = D / 4;
     asm volatile("cp.async.wait_all;" ::: "memory");  // this item's first key tile, staged during the QKV phase
@@ -654,45 +805,47 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         mll[g * 64 + sidx] = ml.y;
     }
     constexpr int kMaxPV = 24;
+    // outputs in rounds of one per thread; a round's loads of every split are issued together
+    const int rounds = (i1 - i0 + kStepConsumers - 1) / kStepConsumers;
     float pv[kMaxPV];
-    const int oi = i0 + tid;  // one output per thread (per <= 256 whenever ns >= 2 for G*D <= 512)
-    const bool mine = oi < i1 && ns <= kMaxPV;
-    if (mine) {
-        const float *po = a.part_o + (size_t)(kvh * G + oi / D) * ns * D + oi % D;
+    for (int rd = 0; rd < rounds; rd++) {
+        const int oi = i0 + rd * kStepConsumers + tid;
+        const bool mine = oi < i1;
+        if (mine && ns <= kMaxPV) {
+            const float *po = a.part_o + (size_t)(kvh * G + oi / D) * ns * D + oi % D;
 #pragma unroll
-        for (int sidx = 0; sidx < kMaxPV; sidx++) pv[sidx] = sidx < ns ? __ldcg(po + (size_t)sidx * D) : 0.f;
-    }
-    consumers_sync();
-    if (tid <= g1 - g0) {
-        const int g = g0 + tid;
-        float M = -INFINITY;
-        for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[g * 64 + sidx]);
-        float L = 0.f;
-        for (int sidx = 0; sidx < ns; sidx++) {
-            const float pm = mlm[g * 64 + sidx];
-            const float e = pm == -INFINITY ? 0.f : expf(pm - M);
-            L += mll[g * 64 + sidx] * e;
-            mlm[g * 64 + sidx] = e;
+            for (int sidx = 0; sidx < kMaxPV; sidx++) pv[sidx] = sidx < ns ? __ldcg(po + (size_t)sidx * D) : 0.f;
         }
-        const float inv = 1.0f / L;
-        for (int sidx = 0; sidx < ns; sidx++) mlm[g * 64 + sidx] *= inv;
-    }
-    consumers_sync();
-    if (mine) {
+        if (rd == 0) {
+            consumers_sync();  // the (max, sum) loads above are in shared memory
+            if (tid <= g1 - g0) {
+                const int g = g0 + tid;
+                float M = -INFINITY;
+                for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[g * 64 + sidx]);
+                float L = 0.f;
+                for (int sidx = 0; sidx < ns; sidx++) {
+                    const float pm = mlm[g * 64 + sidx];
+                    const float e = pm == -INFINITY ? 0.f : expf(pm - M);
+                    L += mll[g * 64 + sidx] * e;
+                    mlm[g * 64 + sidx] = e;
+                }
+                const float inv = 1.0f / L;
+                for (int sidx = 0; sidx < ns; sidx++) mlm[g * 64 + sidx] *= inv;
+            }
+            consumers_sync();
+        }
+        if (!mine) continue;
         const int g = oi / D;
         float O = 0.f;
+        if (ns <= kMaxPV) {
 #pragma unroll
-        for (int sidx = 0; sidx < kMaxPV; sidx++)
-            if (sidx < ns) O += mlm[g * 64 + sidx] * pv[sidx];
-        a.attn[(size_t)kvh * G * D + oi] = O;
-    } else if (ns > kMaxPV) {
-        for (int o = i0 + tid; o < i1; o += kStepConsumers) {
-            const int g = o / D;
-            const float *po = a.part_o + (size_t)(kvh * G + g) * ns * D + o % D;
-            float O = 0.f;
+            for (int sidx = 0; sidx < kMaxPV; sidx++)
+                if (sidx < ns) O += mlm[g * 64 + sidx] * pv[sidx];
+        } else {
+            const float *po = a.part_o + (size_t)(kvh * G + g) * ns * D + oi % D;
             for (int sidx = 0; sidx < ns; sidx++) O += mlm[g * 64 + sidx] * __ldcg(po + (size_t)sidx * D);
-            a.attn[(size_t)kvh * G * D + o] = O;
         }
+        a.attn[(size_t)kvh * G * D + oi] = O;
     }
 }
 
@@ -704,7 +857,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
     __shared__ float red[kStepConsumerWarps], red2[kStepConsumerWarps];
     __shared__ float am_v[kStepConsumers];
     __shared__ int am_i[kStepConsumers];
-    __shared__ int s_last;
     uint8_t *ring = smem;                                            // kRing * kPiece
     float *xs = reinterpret_cast<float *>(smem + kRing * kPiece);    // max K floats
     float *acc = xs + a.xs_floats;                                   // max rows per CTA
@@ -753,8 +905,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
 
     // ======================= consumers =======================
     unsigned target = 0;
+    unsigned gen = *a.gen;            // cross-rank barriers passed so far (monotonic across steps)
+    const unsigned lbase = *a.layers_done;  // layers run by earlier steps (QK-norm sum slots alternate)
     int r0, r1;
     const int token = *a.tokens;
+    const bool tpm = a.tp > 1;
+    const int box_o = kXRows, box_d = kXRows + a.tp * D_;
+    float *xcur = a.x, *xnext = a.x2;  // residual stream (ping-pong under tensor parallelism)
     if (a.trace && blockIdx.x == 0 && tid == 0) a.trace[0] = trace_ns();
     for (int l = 0; l < a.layers; l++) {
         const StepLayer &Ly = a.L[l];
@@ -763,7 +920,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             const __nv_bfloat16 *er = a.embed + (size_t)token * D_;
             for (int k = tid; k < D_; k += kStepConsumers) {
                 const float v = __bfloat162float(er[k]);
-                if (blockIdx.x == 0) a.x[k] = v;
+                if (blockIdx.x == 0) xcur[k] = v;
                 xs[k] = v;
             }
             consumers_sync();
@@ -778,8 +935,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             const float sc = 1.0f / sqrtf(tot / (float)D_ + a.eps);
             for (int k = tid; k < D_; k += kStepConsumers) xs[k] = Ly.rms_att[k] * xs[k] * sc;
             consumers_sync();
+        } else if (tpm) {
+            load_resid(a, xs, xcur, box_d, xnext, Ly.rms_att, red);
+            float *t = xcur; xcur = xnext; xnext = t;
         } else {
-            load_vec(xs, a.x, D_, Ly.rms_att, a.eps, red);
+            load_vec(xs, xcur, D_, Ly.rms_att, a.eps, red);
         }
         {
             // start fetching this CTA's attention keys now: they land behind the QKV weight stream
@@ -807,16 +967,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
                 sk = warp_sum(sk);
                 if (lane == 0) { red[warp] = sq; red2[warp] = sk; }
                 consumers_sync();
-                if (tid == 0) {
-                    float tq = 0.f, tk = 0.f;
-                    for (int w = 0; w < kStepConsumerWarps; w++) { tq += red[w]; tk += red2[w]; }
+                float tq = 0.f, tk = 0.f;
+                for (int w = 0; w < kStepConsumerWarps; w++) { tq += red[w]; tk += red2[w]; }
+                sq = tq;
+                sk = tk;
+                if (tid == 0 && !tpm) {
                     if (tq != 0.f) atomicAdd(a.ss + 2 * l, tq);
                     if (tk != 0.f) atomicAdd(a.ss + 2 * l + 1, tk);
                 }
             }
+            if (tpm && a.qk_mode == 1) {
+                // the accumulator slot the next layer uses was last read two layers ago: clear it now
+                // (slots alternate by the global layer count, which continues across steps)
+                if (blockIdx.x == 0 && tid == 0) {
+                    float *nxt = reinterpret_cast<float *>(a.xch[a.rank]) + kXSs + 2 * ((lbase + l + 1) & 1);
+                    nxt[0] = 0.f;
+                    nxt[1] = 0.f;
+                }
+                if (!cross_sync(a, target, gen, PUB_SS, lbase + l, sq, sk, abort_flag)) break;
+            } else if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) {
+                break;
+            }
         }
-        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
-        // ---- attention ----
+        // ---- attention (this rank's heads) ----
         {
             const int n = *a.positions + 1;
             const int ns = attn_splits(gridDim.x, a.Hkv, n);
@@ -824,25 +997,38 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
                 attn_item<KT, D, G>(a, Ly, l, blockIdx.x / ns, blockIdx.x % ns, ns, scratch, stage);
         }
         if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
-        // ---- O projection + residual ----
+        // ---- O projection + residual (summed over ranks through the inboxes) ----
         load_vec(xs, a.attn, Q, nullptr, 0.f, red);
         if (!consume(rg, D_, Q, xs, acc, r0, r1, abort_flag, a.err)) break;
-        for (int r = tid; r < r1 - r0; r += kStepConsumers) a.x[r0 + r] = __ldcg(a.x + r0 + r) + acc[r];
-        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
-        // ---- rmsnorm + gate/up (raw) ----
-        load_vec(xs, a.x, D_, Ly.rms_ffn, a.eps, red);
+        if (tpm) {
+            push_partial(a, box_o, r0, r1, acc);
+            if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
+            load_resid(a, xs, xcur, box_o, xnext, Ly.rms_ffn, red);
+            float *t = xcur; xcur = xnext; xnext = t;
+        } else {
+            for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
+            if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+            load_vec(xs, xcur, D_, Ly.rms_ffn, a.eps, red);
+        }
+        // ---- gate/up (raw) ----
         if (!consume(rg, 2 * F, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
         for (int r = tid; r < r1 - r0; r += kStepConsumers) a.gu[r0 + r] = acc[r];
         if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
         // ---- SwiGLU (rows interleaved 16 gate / 16 up) + down + residual ----
         load_swiglu(xs, a.gu, F);
         if (!consume(rg, D_, F, xs, acc, r0, r1, abort_flag, a.err)) break;
-        for (int r = tid; r < r1 - r0; r += kStepConsumers) a.x[r0 + r] = __ldcg(a.x + r0 + r) + acc[r];
-        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        if (tpm) {
+            push_partial(a, box_d, r0, r1, acc);
+            if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
+        } else {
+            for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
+            if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        }
     }
     if (*abort_flag) return;
-    // ---- final rmsnorm + lm_head + argmax ----
-    load_vec(xs, a.x, D_, a.norm_final, a.eps, red);
+    // ---- final rmsnorm + lm_head (this rank's vocabulary rows) + argmax ----
+    if (tpm) load_resid(a, xs, xcur, box_d, xnext, a.norm_final, red);
+    else load_vec(xs, xcur, D_, a.norm_final, a.eps, red);
     if (!consume(rg, a.V, D_, xs, acc, r0, r1, abort_flag, a.err)) return;
     if (a.trace && blockIdx.x == 0 && tid == 0) a.trace[2 * (target / gridDim.x) + 1] = trace_ns();
     float bv = -FLT_MAX;
@@ -866,21 +1052,61 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
         }
         if (tid == 0) {
             a.am_val[blockIdx.x] = bv;
-            a.am_idx[blockIdx.x] = bi;
+            a.am_idx[blockIdx.x] = bi + a.v0;
             __threadfence();
-            s_last = atomicAdd(a.am_counter, 1u) == gridDim.x - 1;
+            atomicAdd(a.bar, 1u);
         }
     }
-    consumers_sync();
-    if (!s_last) return;
+    // CTA 0 gathers every CTA's winner, then (tensor parallel) every rank's, and feeds the token back
+    if (blockIdx.x != 0 || warp != 0) return;
+    target += gridDim.x;
+    bool ok = true;
+    if (lane == 0) {
+        const uint64_t t0 = now_ns();
+        while (ld_acquire(a.bar) < target)
+            if (now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     __threadfence();
-    if (tid < 32) {
+    bv = -FLT_MAX;
+    bi = INT_MAX;
+    for (int c = lane; c < (int)gridDim.x; c += 32) {
+        const float v = __ldcg(a.am_val + c);
+        const int i = __ldcg(a.am_idx + c);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (tpm) {
+        // one more flat barrier in which only CTA 0 of each rank takes part: its counter slot grows
+        // by gridDim.x so that the counters stay multiples of the grid
+        gen += 1u;
+        if (lane == 0 && ok) {
+            for (int p = 0; p < a.tp; p++) {
+                unsigned *in = a.xch[p] + kXAm + 2 * a.rank;
+                in[0] = __float_as_uint(bv);
+                in[1] = (unsigned)bi;
+            }
+            __threadfence_system();
+            for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, gridDim.x);
+            const unsigned want = gen * gridDim.x;
+            const unsigned *mine = a.xch[a.rank] + kXFlags;
+            const uint64_t t0 = now_ns();
+            for (int p = 0; ok && p < a.tp; p++)
+                while ((int)(ld_acquire_sys(mine + p) - want) < 0)
+                    if (now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         bv = -FLT_MAX;
         bi = INT_MAX;
-        for (int c = tid; c < (int)gridDim.x; c += 32) {
-            const float v = __ldcg(a.am_val + c);
-            const int i = __ldcg(a.am_idx + c);
-            if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+        if (lane < a.tp) {
+            const unsigned *in = a.xch[a.rank] + kXAm + 2 * lane;
+            bv = __uint_as_float(__ldcg(in));
+            bi = (int)__ldcg(in + 1);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -888,15 +1114,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
-        if (tid == 0) {
-            if (a.argmax_out) *a.argmax_out = bi;
-            if (a.hist) a.hist[*a.positions + 1] = bi;
-            if (a.advance) {
-                *a.tokens = bi;
-                *a.positions += 1;
-            }
-            *a.am_counter = 0u;
+    }
+    if (lane == 0) {
+        if (!ok) {
+            atomicExch(a.err, 5);
+            return;
         }
+        if (a.argmax_out) *a.argmax_out = bi;
+        if (a.hist) a.hist[*a.positions + 1] = bi;
+        if (a.advance) {
+            *a.tokens = bi;
+            *a.positions += 1;
+        }
+        *a.gen = gen;
+        *a.layers_done = lbase + a.layers;
     }
 }
 
@@ -927,7 +1158,7 @@ size_t step_smem_bytes(const StepArgs &a) {
 
 bool step_layout(StepArgs &a, int grid, size_t *smem_out) {
     const int Q = a.H * a.d, KVw = a.Hkv * a.d, G = a.H / a.Hkv;
-    if (a.D % 1024 || Q % 1024 || a.F % 1024) return false;
+    if (a.D % 512 || Q % 512 || a.F % 512) return false;
     if (a.d != 64 && a.d != 128) return false;
     if (G != 1 && G != 2 && G != 4 && G != 8) return false;
     a.max_k = std::max(a.D, std::max(Q, a.F));

@@ -190,7 +190,8 @@ qw_status qw_set_device_inputs(qw_model *m, const int32_t *tokens, const int32_t
 qw_status qw_profile_decode(qw_model *m, int32_t batch, float *ms_out, int32_t *kinds_out, int32_t cap,
                             int32_t *n_out);
 
-/* Wait for all work on the model's stream. */
+/* Wait for all work on the model's stream; QW_ERR_TIMEOUT if a bounded device-side wait gave up
+ * since the model was created (a peer rank that never arrived, for instance). */
 qw_status qw_synchronize(qw_model *m);
 
 /* The model's CUDA stream (cudaStream_t) for event timing by the caller. */

@@ -11,11 +11,14 @@ pytestmark = pytest.mark.gpu
 BF16_TOL = 2e-2
 
 
+# every geometry here runs the step kernel (dim, heads*head_dim and intermediate multiples of 512);
+# each test checks that one decode step is one kernel launch
 @pytest.mark.parametrize("variant", [
-    dict(),                                                            # d 64, G 2, whole-vector QK-norm
-    dict(head_dim=128, dim=512, heads=8, kv_heads=2, hidden_dim=1024),  # d 128, G 4
-    dict(qk_norm=2, has_qkv_bias=1, heads=8, kv_heads=1, dim=512),     # per-head norm, biases, G 8
-    dict(shared_weights=1, heads=4, kv_heads=4),                        # tied lm_head, G 1
+    dict(dim=512, hidden_dim=1024, heads=8, kv_heads=4, head_dim=64),                   # d 64, G 2, vector QK-norm
+    dict(dim=1024, hidden_dim=2048, heads=8, kv_heads=2, head_dim=128),                 # d 128, G 4
+    dict(qk_norm=2, has_qkv_bias=1, dim=1024, hidden_dim=1536, heads=8, kv_heads=1,
+         head_dim=128),                                                                  # per-head, biases, G 8, K 1536
+    dict(shared_weights=1, dim=512, hidden_dim=512, heads=8, kv_heads=8, head_dim=64),  # tied lm_head, G 1
 ])
 def test_step_kernel_matches_oracle_long_context(variant):
     """300 positions: the attention phase splits the context over up to 64 CTAs per KV head."""
@@ -27,6 +30,7 @@ def test_step_kernel_matches_oracle_long_context(variant):
     worst = 0.0
     for p, t in enumerate(toks):
         lg, am = m.decode_step([int(t)], [p])
+        assert m.last_launch_count == 1  # the persistent step kernel, not one kernel per op
         want = o.forward_token(int(t), p)
         if p % 10 == 0 or p > 290:
             worst = max(worst, rel_l2(lg[0], want))
@@ -37,14 +41,16 @@ def test_step_kernel_matches_oracle_long_context(variant):
 
 
 def test_step_kernel_equals_per_op_path():
-    c = cfg_dict(seq_len=64, head_dim=128, dim=512, heads=8, kv_heads=2, hidden_dim=1024)
+    c = cfg_dict(seq_len=64, head_dim=128, dim=1024, heads=8, kv_heads=2, hidden_dim=2048)
     sd = state_dict(c, seed=42, std=0.05, norm_noise=0.1)
     a = native_model(c, sd, precision="bf16", decode_kernels=0)
     b = native_model(c, sd, precision="bf16", decode_kernels=1)
     toks = np.random.default_rng(43).integers(0, c["vocab"], 40)
     for p, t in enumerate(toks):
         la, ia = a.decode_step([int(t)], [p])
+        assert a.last_launch_count == 1
         lb, ib = b.decode_step([int(t)], [p])
+        assert b.last_launch_count > 1
         assert rel_l2(la[0], lb[0]) < 1e-4, p  # same math, different summation order
     a.close()
     b.close()
@@ -52,7 +58,7 @@ def test_step_kernel_equals_per_op_path():
 
 def test_step_kernel_generate_and_graph():
     """qw_generate (device-resident token feedback) and graph replay through the step kernel."""
-    c = cfg_dict(seq_len=64, vocab=500)
+    c = cfg_dict(seq_len=64, vocab=500, dim=512, hidden_dim=1024, heads=8, kv_heads=4, head_dim=64)
     sd = state_dict(c, seed=44, std=0.08, norm_noise=0.1)
     prompt = np.random.default_rng(45).integers(0, c["vocab"], 8)
     m = native_model(c, sd, precision="bf16")
@@ -66,7 +72,7 @@ def test_step_kernel_generate_and_graph():
 
 def test_step_kernel_graph_replay_equals_eager():
     import torch
-    c = cfg_dict(seq_len=64)
+    c = cfg_dict(seq_len=64, dim=512, hidden_dim=1024, heads=8, kv_heads=4, head_dim=64)
     sd = state_dict(c, seed=46, std=0.08)
     a = native_model(c, sd, precision="bf16")
     b = native_model(c, sd, precision="bf16")

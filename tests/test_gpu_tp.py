@@ -21,7 +21,7 @@ def test_tp2_matches_oracle():
     from common_b200 import native
     from tests.tp_worker import run_rank
     c = cfg_dict(seq_len=64)
-    nids = [native.unique_id(), native.unique_id()]  # one communicator per model
+    nids = [native.unique_id() for _ in range(3)]  # one communicator per model
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=run_rank, args=(r, 2, nids, c, q)) for r in range(2)]
@@ -57,5 +57,18 @@ def test_tp2_matches_oracle():
             want = ob.forward_token(int(seqs[b, p]), p)
         assert rel_l2(out["batch6"][b], want) < 2e-2
         ob.close()
+    # greedy tokens of the tensor-parallel step kernel: the oracle's argmax at every step, or a near-tie
+    assert out["step_launches"] == 1
+    got = out["greedy"]
+    np.testing.assert_array_equal(res[1]["greedy"], got)
+    from tests.tp_worker import step_cfg
+    c2, sd2 = step_cfg()
+    ob = oracle_model(c2, sd2, bf16_weights=True)
+    for p in range(len(got) - 1):
+        lg = ob.forward_token(int(got[p]), p)
+        if p >= 7 and int(np.argmax(lg)) != int(got[p + 1]):
+            assert lg.max() - lg[int(got[p + 1])] < 2e-2 * lg.std(), p
+    ob.close()
+    assert out["graph"] == [int(t) for t in got[9:]]
     # both ranks return the full (gathered) logits
     np.testing.assert_allclose(res[1]["fp32"][5], out["fp32"][5], rtol=1e-5, atol=1e-6)

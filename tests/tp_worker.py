@@ -3,6 +3,13 @@ own NCCL unique id: an id bootstraps exactly one communicator."""
 import numpy as np
 
 
+def step_cfg():
+    """A geometry the persistent step kernel runs at tp 2: dim, local q width and intermediate multiples of 512."""
+    from tests.helpers import cfg_dict, state_dict
+    c = cfg_dict(dim=1024, hidden_dim=2048, layers=2, heads=8, kv_heads=2, head_dim=128, vocab=2000, seq_len=64)
+    return c, state_dict(c, seed=54, std=0.05, norm_noise=0.1)
+
+
 def run_rank(rank, world, nids, c, q):
     try:
         from common_b200 import native
@@ -23,6 +30,29 @@ def run_rank(rank, world, nids, c, q):
         for p in range(5):
             last = m.decode_step(seqs[:, p].tolist(), [p] * 6, slots=[2, 3, 4, 5, 6, 7])[0]
         out["batch6"] = last
+        m.close()
+        # bf16 batch-1 greedy generation: the persistent step kernel with the cross-rank exchange over NVLink
+        c, sd = step_cfg()
+        m = native_model_tp(c, sd, "bf16", rank, world, nids[2], max_batch=1, max_tokens=8)
+        out["greedy"] = m.generate(np.array([3, 1, 4, 1, 5, 9, 2, 6], np.int32), 8 + 24)[0]
+        out["step_launches"] = m.last_launch_count  # 1: the persistent step kernel ran
+        # the same greedy steps replayed from a captured CUDA graph (token/position advance on the device)
+        import torch
+        torch.cuda.set_device(rank)
+        m.reset()
+        m.prefill(np.array([[3, 1, 4, 1, 5, 9, 2, 6]], np.int32), want_logits=False)
+        m.reserve(0, 40)
+        dt = torch.tensor([int(out["greedy"][8])], dtype=torch.int32, device="cuda")
+        dp = torch.tensor([8], dtype=torch.int32, device="cuda")
+        ds = torch.zeros(1, dtype=torch.int32, device="cuda")
+        dam = torch.zeros(1, dtype=torch.int32, device="cuda")
+        m.capture_decode(dt.data_ptr(), ds.data_ptr(), dp.data_ptr(), 1, 0, dam.data_ptr())
+        graph = []
+        for _ in range(23):
+            m.replay_decode(1)
+            m.synchronize()
+            graph.append(int(dt.item()))
+        out["graph"] = graph
         m.close()
         q.put((rank, out, None))
     except Exception as e:  # report instead of hanging the parent
