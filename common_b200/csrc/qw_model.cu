@@ -911,7 +911,9 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
         CK(tc_prepare());
         CK(prefill_kernels_prepare());
     }
-    if (m->bf16w && c.decode_kernels == 0) {
+    // the persistent step kernel: automatic at tp 1; under tensor parallelism only when asked for
+    // (decode_kernels 2), its cross-GPU barriers cost more than the NCCL path saves at these sizes
+    if (m->bf16w && (c.decode_kernels == 2 || (c.decode_kernels == 0 && tp_size == 1))) {
         StepArgs &sa = m->step;
         sa.layers = c.layers; sa.D = D; sa.F = m->Fl; sa.V = m->Vl; sa.H = m->Hl; sa.Hkv = m->Hkvl; sa.d = c.head_dim;
         sa.kv_bf16 = m->bf16kv;

@@ -317,9 +317,8 @@ __device__ __forceinline__ void red_release_sys(unsigned *p, unsigned v) {
 // What every CTA adds to every rank's exchange buffer before arriving at a cross-rank barrier.
 enum { PUB_NONE = 0, PUB_SS = 1 };
 
-// Barrier over every CTA of every tensor-parallel rank, flat: each CTA fences its stores (including
-// the NVLink stores into the peers' inboxes) at system scope and adds one, with release semantics, to
-// its rank's arrival counter in every rank's exchange buffer; then every CTA waits until the counters
+// Barrier over every CTA of every tensor-parallel rank, flat: each CTA adds one, with system-scope
+// release semantics, to its rank's arrival counter in every rank's exchange buffer; then every CTA waits until the counters
 // in its own GPU's buffer show all CTAs of all ranks.  Counters grow monotonically across barriers
 // and steps (gen = barriers passed so far), compared with wrap-around arithmetic.  PUB_SS also adds
 // this CTA's q / k sums of squares into every rank's per-layer accumulator.
@@ -338,7 +337,8 @@ __device__ __forceinline__ bool cross_sync(const StepArgs &a, unsigned &target, 
                 atomicAdd(acc2, sq);
                 atomicAdd(acc2 + 1, sk);
             }
-        __threadfence_system();
+        // release at system scope after the CTA barrier orders every thread's stores (the NVLink
+        // stores into the peers' inboxes included) before the arrival
         for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, 1u);
         const unsigned want = gen * gridDim.x;
         const unsigned *mine = a.xch[a.rank] + kXFlags;

@@ -76,8 +76,10 @@ typedef struct qw_config {
     int32_t max_tokens;     /* max tokens in one prefill call (activation arena), >= max_batch */
     int32_t page_size;      /* KV page size in tokens (power of two, 16..256); 0 = 64 */
     int32_t num_pages;      /* KV pages per rank; 0 = max_batch * ceil(seq_len / page_size) */
-    int32_t decode_kernels; /* batch-1 decode at tp 1 with bf16 weights: 0 = one persistent kernel per step
-                               (auto), 1 = one kernel per operation */
+    int32_t decode_kernels; /* batch-1 decode with bf16 weights: 0 = auto (one persistent kernel per step at
+                               tp 1, one kernel per operation + NCCL under tensor parallelism), 1 = one
+                               kernel per operation, 2 = the persistent kernel at any tp (cross-GPU
+                               exchange over NVLink peer memory) */
     int32_t reserved[4];
     double rope_theta;      /* 1e6 for Qwen3 */
     double eps;             /* rmsnorm epsilon, 1e-6 for Qwen3 */

@@ -84,13 +84,13 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def native_model_tp(c, sd, precision, rank, world, nid, max_batch=1, max_tokens=0, page_size=64):
+def native_model_tp(c, sd, precision, rank, world, nid, max_batch=1, max_tokens=0, page_size=64, decode_kernels=0):
     """One tensor-parallel rank (device = rank) holding its shard of the state dict."""
     dt = {"fp32": native.DTYPE_F32, "bf16": native.DTYPE_BF16}
     cfg = native.make_config(c["dim"], c["hidden_dim"], c["layers"], c["heads"], c["kv_heads"], c["head_dim"],
                              c["vocab"], c["seq_len"], c["shared_weights"], c["qk_norm"], c["has_qkv_bias"],
                              dt[precision], dt[precision], max_batch, max_tokens, page_size, 0,
-                             c["rope_theta"], c["eps"])
+                             c["rope_theta"], c["eps"], decode_kernels)
     m = native.NativeModel(cfg, rank, rank, world, nid)
     for k, v in sd.items():
         m.load_tensor(k, v)

@@ -33,7 +33,7 @@ def run_rank(rank, world, nids, c, q):
         m.close()
         # bf16 batch-1 greedy generation: the persistent step kernel with the cross-rank exchange over NVLink
         c, sd = step_cfg()
-        m = native_model_tp(c, sd, "bf16", rank, world, nids[2], max_batch=1, max_tokens=8)
+        m = native_model_tp(c, sd, "bf16", rank, world, nids[2], max_batch=1, max_tokens=8, decode_kernels=2)
         out["greedy"] = m.generate(np.array([3, 1, 4, 1, 5, 9, 2, 6], np.int32), 8 + 24)[0]
         out["step_launches"] = m.last_launch_count  # 1: the persistent step kernel ran
         # the same greedy steps replayed from a captured CUDA graph (token/position advance on the device)
