@@ -257,7 +257,7 @@ def run_ours(args):
     seq_len = PROMPT + args.warmup + args.steps + e2e_steps + 8
     cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
                              g["vocab"], seq_len, False, native.QKNORM_VECTOR, False, native.DTYPE_BF16,
-                             native.DTYPE_BF16, B, 0)
+                             native.DTYPE_BF16, B, PROMPT)  # the prompt is one tensor-core prefill chunk
     m = native.NativeModel(cfg, local, rank, world, nid)
     m.init_synthetic(0, 0.02)
     m.finalize()
@@ -391,6 +391,64 @@ def run_ours(args):
     return 0
 
 
+def run_case(args):
+    """Small fixed workloads for profiler captures (a few GB on the device, few launches):
+      step-small  the 8B geometry cut to --layers layers, 4 batch-1 decode steps (the persistent step kernel)
+      gemm        one qw_op_linear GEMM (--gemm M K T EPI) timed with CUDA events
+      attn-b64    the 8B geometry cut to 2 layers, 64 sequences prefilled to 2048 tokens, 3 batch-64 decode steps
+    """
+    import numpy as np
+    from common_b200 import build, native
+    build.build()
+    g = GEOM_8B
+    if args.case == "gemm":
+        import torch
+        M, K, T, epi = args.gemm
+        W = (torch.randn(M, K, device="cuda") * 0.02).bfloat16()
+        X = torch.randn(T, K, device="cuda").bfloat16()
+        out = torch.zeros(T, M // 2 if epi == 2 else M, device="cuda",
+                          dtype=torch.bfloat16 if epi == 2 else torch.float32)
+
+        def once():
+            native.op_linear(W.data_ptr(), M, K, X.data_ptr(), T, epi, 0, out.data_ptr() if epi == 1 else 0,
+                             out.data_ptr())
+        for _ in range(3):
+            once()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            once()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        print(json.dumps({"case": "gemm", "M": M, "K": K, "T": T, "epi": epi, "ms": ms,
+                          "tflops": 2.0 * M * K * T / ms / 1e9}))
+        return 0
+    layers = args.layers if args.case == "step-small" else 2
+    B, L = (1, 1024) if args.case == "step-small" else (64, 2048)
+    cfg = native.make_config(g["dim"], g["hidden_dim"], layers, g["heads"], g["kv_heads"], g["head_dim"], g["vocab"],
+                             L + 16, False, native.QKNORM_VECTOR, False, native.DTYPE_BF16, native.DTYPE_BF16, B,
+                             16384 if B > 1 else 0)
+    m = native.NativeModel(cfg, 0)
+    m.init_synthetic(0, 0.02)
+    m.finalize()
+    if args.case == "step-small":
+        for p in range(4):
+            m.decode_step([5], [p], want_logits=False)
+    else:
+        prompts = np.random.default_rng(1).integers(0, g["vocab"], (B, L)).astype(np.int32)
+        for c0 in range(0, B, 8):
+            m.prefill(prompts[c0:c0 + 8], slots=np.arange(c0, c0 + 8, dtype=np.int32), want_logits=False)
+        toks = np.random.default_rng(2).integers(0, g["vocab"], B)
+        for st in range(3):
+            m.decode_step(toks.tolist(), [L + st] * B, want_logits=False)
+    m.synchronize()
+    m.close()
+    print(json.dumps({"case": args.case, "ok": True}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -405,12 +463,17 @@ def main():
     ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--decode-batch", type=int, default=64)
     ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--case", choices=["step-small", "gemm", "attn-b64"], help="a small profiler workload instead")
+    ap.add_argument("--layers", type=int, default=4, help="--case step-small: layers of the cut 8B model")
+    ap.add_argument("--gemm", type=int, nargs=4, default=[24576, 4096, 4096, 2], metavar=("M", "K", "T", "EPI"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt-len", type=int, default=PROMPT, help="shorter prompts for profiler runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     globals()["PROMPT"] = args.prompt_len
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -68,6 +68,9 @@ def _compile(src, verbose=False):
 def build(verbose: bool = False) -> str:
     os.makedirs(OBJDIR, exist_ok=True)
     srcs = _sources()
+    # an up-to-date library needs no objects (they are not shipped with a copy of the tree)
+    if not verbose and os.path.exists(LIB) and not _stale(LIB, srcs + _headers()):
+        return LIB
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         results = list(ex.map(lambda s: _compile(s, verbose), srcs))
     objs = [o for o, _ in results]

@@ -166,9 +166,9 @@ struct StepArgs {
 size_t step_smem_bytes(const StepArgs &a);
 // Fills a.max_k / max_rows / xs_floats; false when the geometry or shared memory does not fit.
 bool step_layout(StepArgs &a, int grid, size_t *smem_out);
-cudaError_t step_prepare(bool kv_bf16, int d, int G, size_t smem);
+cudaError_t step_prepare(bool kv_bf16, int d, int G, bool tp, size_t smem);
 cudaError_t step_launch(const StepArgs &a, bool kv_bf16, int grid, cudaStream_t st);
-const void *step_kernel_fn(bool kv_bf16, int d, int G);
+const void *step_kernel_fn(bool kv_bf16, int d, int G, bool tp);
 constexpr int kStepBlockThreads = 288;
 
 cudaError_t gemv_launch(const GemvArgs &a, int epi, bool bf16, int num_sms, cudaStream_t st);

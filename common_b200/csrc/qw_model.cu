@@ -921,10 +921,10 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
         int coop = 0;
         CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
         if (coop && step_layout(sa, m->num_sms, &smem)) {
-            CK(step_prepare(m->bf16kv, c.head_dim, m->Hl / m->Hkvl, smem));
+            CK(step_prepare(m->bf16kv, c.head_dim, m->Hl / m->Hkvl, tp_size > 1, smem));
             int occ = 0;
-            CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel_fn(m->bf16kv, c.head_dim, m->Hl / m->Hkvl),
-                                                             kStepBlockThreads, smem));
+            CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &occ, step_kernel_fn(m->bf16kv, c.head_dim, m->Hl / m->Hkvl, tp_size > 1), kStepBlockThreads, smem));
             if (occ >= 1) {
                 m->use_step = true;
                 sa.norm_final = m->norm_final; sa.eps = (float)c.eps; sa.scale = (float)(1.0 / sqrt((double)c.head_dim));

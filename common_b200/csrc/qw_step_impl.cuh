@@ -1,0 +1,1155 @@
+// qw_step_impl.cuh -- the whole batch-1 decode step as one persistent kernel (included by qw_step.cu,
+// which instantiates it for tp = 1, and qw_step_tp.cu, which instantiates the tensor-parallel variants).
+//
+// Batch-1 decode streams every weight byte once per token; its speed is set by how close the
+// weight stream stays to HBM bandwidth.  Launching one kernel per projection loses that at every
+// boundary (ramp-up, tail, prologue), so here one CTA per SM runs the full step
+// (Qwen3.java:334-415: L x [rmsnorm, QKV, QK-norm, RoPE, KV write, attention, O + residual,
+// rmsnorm, gate/up, SwiGLU, down + residual], final rmsnorm, lm_head, greedy argmax):
+//
+//   warp 8 (producer)   streams this CTA's contiguous share of every weight matrix of the step,
+//                       in step order, into a ring of 16 KiB shared-memory slots with
+//                       cp.async.bulk (no multicast).  It only waits for free slots, never for
+//                       activations, so HBM keeps streaming the next phase's weights while the
+//                       consumers sit in a grid barrier or in the attention phase.
+//   warps 0-7           consume the slots: 8-element bf16 x fp32 dot products against the phase's
+//                       activation vector (fp32, in shared memory), per-row partial sums in
+//                       shared memory, the phase epilogue, then a grid barrier.
+//
+// Phases per layer: QKV (rows split over CTAs) | attention (work items = KV head x context
+// split, merged by the last CTA of each KV head) | O + residual | gate/up (raw, SwiGLU is
+// applied by the next phase's loader) | down + residual.  Then lm_head with a first-index-of-max
+// reduction (AggregationFeatures.java:111-121) merged by the last CTA, which also feeds the
+// token back and advances the position (AutoregressiveModel.java:295-308).
+//
+// Data written by one CTA and read by another after a grid barrier is read with ld.global.cg
+// (L2), never through L1.  Every wait (slot barriers, grid barriers) is bounded by time: on
+// expiry the kernel records an error, stops, lets its issued copies land and returns.
+#pragma once
+#include "qw_internal.cuh"
+#include "qw_kernels.h"
+#include <float.h>
+#include <limits.h>
+#include <algorithm>
+
+namespace qw {
+
+namespace {
+
+constexpr int kStepConsumerWarps = 8;
+constexpr int kStepConsumers = kStepConsumerWarps * 32;
+constexpr int kStepThreads = kStepConsumers + 32;
+static_assert(kStepThreads == kStepBlockThreads, "block size");
+constexpr int kRows = 4;        // weight rows per ring slot
+constexpr int kPiece = 32768;  // bytes per ring slot (kRows rows x up to 4096 columns)
+constexpr int kRing = 5;
+constexpr unsigned long long kStepWaitNs = 4000ull * 1000ull * 1000ull;  // cycles: ~2 s at 2 GHz
+// layout of a rank's exchange buffer (32-bit words): flags, QK-norm sums, argmax, row partials
+constexpr int kXFlags = 0;   // [tp] generation flags, written by each peer
+constexpr int kXSs = 64;     // [2][2] q / k sums of squares accumulated over all ranks (even / odd layers)
+constexpr int kXAm = 96;     // [tp][2] (value, index) of each rank's vocabulary shard
+constexpr int kXRows = 128;  // [2][tp][D]: O partials, then down partials
+constexpr int kStepTPW = 4;  // attention: keys per warp per tile (small: this code runs once per layer, cold in the instruction cache)
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// cycle counter of this SM: cheap to read in a spin loop (the bounds below are in cycles)
+__device__ __forceinline__ uint64_t now_ns() { return (uint64_t)clock64(); }
+// wall-clock nanoseconds (the profiling trace only)
+__device__ __forceinline__ unsigned long long trace_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool mb_try(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+    const uint32_t addr = su32(b);
+    if (mb_try(addr, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (;;) {
+        if (mb_try(addr, parity)) return true;
+        if (*abort_flag) return false;
+        if (now_ns() - t0 > kStepWaitNs) {
+            *abort_flag = 1;
+            atomicExch(err, 1);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kStepConsumers) : "memory"); }
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <typename T>
+__device__ __forceinline__ T ldcg(const T *p) { return __ldcg(p); }
+
+// context splits of the attention phase: at most one work item per CTA, at least 16 keys per split
+__device__ __forceinline__ int attn_splits(int grid, int Hkv, int n) {
+    int ns = min(grid / Hkv, (n + 15) / 16);
+    return max(1, min(ns, 64));
+}
+
+__device__ __forceinline__ void split_rows(int N, int c, int n, int &r0, int &r1) {
+    r0 = (int)(((long long)N * c) / n);
+    r1 = (int)(((long long)N * (c + 1)) / n);
+}
+
+struct Ring {
+    uint64_t *full, *empty;
+    uint8_t *buf;
+    int slot;
+    uint32_t ph;
+};
+
+// Column chunk of one ring slot: a slot holds the same C columns of kRows consecutive rows, so every
+// activation value read from shared memory serves kRows weight rows.
+__host__ __device__ __forceinline__ int chunk_cols(int K) {
+    return (K & 4095) == 0 ? 4096 : ((K & 2047) == 0 ? 2048 : ((K & 1023) == 0 ? 1024 : 512));
+}
+
+// producer: this CTA's rows [r0, r1) of W (N, K), kRows rows at a time, each group in column chunks
+__device__ __forceinline__ bool produce(Ring &rg, const __nv_bfloat16 *W, int N, int K, volatile int *abort_flag,
+                                        int *err, uint32_t &issued, uint32_t &last_ph) {
+    int r0, r1;
+    split_rows(N, blockIdx.x, gridDim.x, r0, r1);
+    const int C = chunk_cols(K);
+    for (int ra = r0; ra < r1; ra += kRows) {
+        const int nr = min(kRows, r1 - ra);
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.empty[rg.slot], rg.ph ^ 1u, abort_flag, err)) return false;
+            const uint32_t fb = su32(&rg.full[rg.slot]);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb), "r"((uint32_t)(nr * C * 2))
+                         : "memory");
+            for (int j = 0; j < nr; j++)
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        su32(rg.buf + (size_t)rg.slot * kPiece + (size_t)j * C * 2)),
+                    "l"(W + (size_t)(ra + j) * K + c0), "r"((uint32_t)(C * 2)), "r"(fb)
+                    : "memory");
+            issued |= 1u << rg.slot;
+            last_ph = (last_ph & ~(1u << rg.slot)) | (rg.ph << rg.slot);
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ float dot4(const uint2 w, const float4 x, float acc) {
+    acc = fmaf(bf16lo(w.x), x.x, acc);
+    acc = fmaf(bf16hi(w.x), x.y, acc);
+    acc = fmaf(bf16lo(w.y), x.z, acc);
+    return fmaf(bf16hi(w.y), x.w, acc);
+}
+
+// Sum four per-lane values over the warp in 6 shuffles: afterwards lane 0 holds the total of v0,
+// lane 8 of v1, lane 16 of v2 and lane 24 of v3.
+__device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v3) {
+    const int lane = threadIdx.x & 31;
+    const bool lo = lane < 16;
+    float x0 = lo ? v0 : v2, x1 = lo ? v1 : v3;
+    const float y0 = lo ? v2 : v0, y1 = lo ? v3 : v1;
+    x0 += __shfl_xor_sync(0xffffffffu, y0, 16);
+    x1 += __shfl_xor_sync(0xffffffffu, y1, 16);
+    const bool lo8 = (lane & 8) == 0;
+    float z = lo8 ? x0 : x1;
+    z += __shfl_xor_sync(0xffffffffu, lo8 ? x1 : x0, 8);
+    z += __shfl_xor_sync(0xffffffffu, z, 4);
+    z += __shfl_xor_sync(0xffffffffu, z, 2);
+    z += __shfl_xor_sync(0xffffffffu, z, 1);
+    return z;
+}
+
+// consumers: acc[r - r0] = W[r, :] . xs for this CTA's rows; returns the row range.  Warp w takes
+// columns [w C/8, (w+1) C/8) of each slot in 128-column steps, lane l columns 4l .. 4l+3 of a step
+// (contiguous 16-byte activation loads, 8-byte weight loads), for all kRows rows of the slot; the
+// partial sums stay in registers until the row group is done.  C is a template argument so the
+// slot loop unrolls completely.
+template <int C>
+__device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+                                          volatile int *abort_flag, int *err) {
+    constexpr int PER_WARP = C / 8;
+    constexpr int STEPS = PER_WARP / 128;
+    static_assert(STEPS >= 1, "C >= 1024 (see consume_512)");
+    static_assert(kRows == 4, "warp_sum4 reduces four rows");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cw = warp * PER_WARP + lane * 4;
+    for (int ra = r0; ra < r1; ra += kRows) {
+        const int nr = min(kRows, r1 - ra);
+        float p[kRows][STEPS];
+#pragma unroll
+        for (int r = 0; r < kRows; r++)
+#pragma unroll
+            for (int j = 0; j < STEPS; j++) p[r][j] = 0.f;
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err)) return false;
+            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
+            const float *xp = xs + c0 + cw;
+            float4 x[STEPS];
+            uint2 w[kRows][STEPS];
+#pragma unroll
+            for (int j = 0; j < STEPS; j++) {
+                x[j] = *reinterpret_cast<const float4 *>(xp + j * 128);
+#pragma unroll
+                for (int r = 0; r < kRows; r++)
+                    w[r][j] = *reinterpret_cast<const uint2 *>(sa + (size_t)r * C * 2 + j * 256);
+            }
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+#pragma unroll
+            for (int j = 0; j < STEPS; j++)
+#pragma unroll
+                for (int r = 0; r < kRows; r++) p[r][j] = dot4(w[r][j], x[j], p[r][j]);
+        }
+        float t[kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; r++) {
+            t[r] = 0.f;
+#pragma unroll
+            for (int j = 0; j < STEPS; j++) t[r] += p[r][j];
+        }
+        const float tot = warp_sum4(t[0], t[1], t[2], t[3]);
+        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
+    }
+    return true;
+}
+
+// C = 512 (K an odd multiple of 512, e.g. a tensor-parallel shard): warp w takes 64 columns of each
+// slot, lane l columns 2l, 2l+1
+__device__ __forceinline__ bool consume_512(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+                                            volatile int *abort_flag, int *err) {
+    constexpr int C = 512;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cw = warp * 64 + lane * 2;
+    for (int ra = r0; ra < r1; ra += kRows) {
+        const int nr = min(kRows, r1 - ra);
+        float p[kRows] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err)) return false;
+            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
+            const float2 x = *reinterpret_cast<const float2 *>(xs + c0 + cw);
+            uint32_t w[kRows];
+#pragma unroll
+            for (int r = 0; r < kRows; r++) w[r] = *reinterpret_cast<const uint32_t *>(sa + (size_t)r * C * 2);
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+#pragma unroll
+            for (int r = 0; r < kRows; r++) p[r] = fmaf(bf16hi(w[r]), x.y, fmaf(bf16lo(w[r]), x.x, p[r]));
+        }
+        const float tot = warp_sum4(p[0], p[1], p[2], p[3]);
+        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool consume(Ring &rg, int N, int K, const float *xs, float *acc, int &r0, int &r1,
+                                        volatile int *abort_flag, int *err) {
+    split_rows(N, blockIdx.x, gridDim.x, r0, r1);
+    const int tid = threadIdx.x;
+    for (int r = tid; r < r1 - r0; r += kStepConsumers) acc[r] = 0.f;
+    consumers_sync();
+    bool ok;
+    switch (chunk_cols(K)) {
+        case 4096: ok = consume_c<4096>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 2048: ok = consume_c<2048>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 1024: ok = consume_c<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        default: ok = consume_512(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+    }
+    if (!ok) return false;
+    consumers_sync();
+    return true;
+}
+
+// every CTA's writes before the barrier are visible to every CTA after it
+__device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned &target, volatile int *abort_flag, int *err,
+                                          unsigned long long *trace = nullptr) {
+    consumers_sync();
+    const unsigned idx = target / gridDim.x;
+    target += gridDim.x;
+    if (threadIdx.x == 0 && trace && blockIdx.x == 0) trace[2 * idx + 1] = trace_ns();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(bar, 1u);
+        const uint64_t t0 = now_ns();
+        while (ld_acquire(bar) < target) {
+            if (*abort_flag || ld_acquire(reinterpret_cast<unsigned *>(err)) != 0u) { *abort_flag = 1; break; }
+            if (now_ns() - t0 > kStepWaitNs) {
+                *abort_flag = 1;
+                atomicExch(err, 2);
+                break;
+            }
+        }
+        __threadfence();
+        if (trace && blockIdx.x == 0) trace[2 * idx + 2] = trace_ns();
+    }
+    consumers_sync();
+    return !*abort_flag;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_release_sys(unsigned *p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// What every CTA adds to every rank's exchange buffer before arriving at a cross-rank barrier.
+enum { PUB_NONE = 0, PUB_SS = 1 };
+
+// Barrier over every CTA of every tensor-parallel rank, flat: each CTA adds one, with system-scope
+// release semantics, to its rank's arrival counter in every rank's exchange buffer; then every CTA waits until the counters
+// in its own GPU's buffer show all CTAs of all ranks.  Counters grow monotonically across barriers
+// and steps (gen = barriers passed so far), compared with wrap-around arithmetic.  PUB_SS also adds
+// this CTA's q / k sums of squares into every rank's per-layer accumulator.
+__device__ __forceinline__ bool cross_sync(const StepArgs &a, unsigned &target, unsigned &gen, int pub, int layer,
+                                           float sq, float sk, volatile int *abort_flag) {
+    consumers_sync();
+    const unsigned idx = target / gridDim.x;
+    target += gridDim.x;
+    gen += 1u;
+    if (threadIdx.x == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 1] = trace_ns();
+    if (threadIdx.x == 0) {
+        atomicAdd(a.bar, 1u);  // keeps the local barrier counter in step with `target`
+        if (pub == PUB_SS)
+            for (int p = 0; p < a.tp; p++) {
+                float *acc2 = reinterpret_cast<float *>(a.xch[p]) + kXSs + 2 * (layer & 1);  // layer: global count
+                atomicAdd(acc2, sq);
+                atomicAdd(acc2 + 1, sk);
+            }
+        // release at system scope after the CTA barrier orders every thread's stores (the NVLink
+        // stores into the peers' inboxes included) before the arrival
+        for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, 1u);
+        const unsigned want = gen * gridDim.x;
+        const unsigned *mine = a.xch[a.rank] + kXFlags;
+        const uint64_t t0 = now_ns();
+        bool ok = true;
+        for (int p = 0; ok && p < a.tp; p++)
+            while ((int)(ld_acquire_sys(mine + p) - want) < 0)
+                if (*abort_flag || now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+        if (!ok) {
+            *abort_flag = 1;
+            atomicExch(a.err, 4);
+        }
+        if (a.trace && blockIdx.x == 0) a.trace[2 * idx + 2] = trace_ns();
+    }
+    consumers_sync();
+    return !*abort_flag;
+}
+
+// this rank's partial of rows [r0, r1) of a row-split projection into inbox slot `rank` of every rank
+__device__ __forceinline__ void push_partial(const StepArgs &a, int box, int r0, int r1, const float *acc) {
+    for (int r = threadIdx.x; r < r1 - r0; r += kStepConsumers) {
+        const float v = acc[r];
+        for (int p = 0; p < a.tp; p++)
+            reinterpret_cast<float *>(a.xch[p])[box + (size_t)a.rank * a.D + r0 + r] = v;
+    }
+}
+
+// xs = rmsnorm(x + sum over ranks of the inbox partials) * w; the rows this CTA owns of the
+// un-normalised sum are written to xnext (the residual stream's other buffer)
+__device__ __forceinline__ void load_resid(const StepArgs &a, float *xs, const float *xcur, int box, float *xnext,
+                                           const float *w, float *red) {
+    const int tid = threadIdx.x, K = a.D;
+    const float *in = reinterpret_cast<const float *>(a.xch[a.rank]) + box;
+    int o0, o1;
+    split_rows(K, blockIdx.x, gridDim.x, o0, o1);
+    float ss = 0.f;
+    for (int q = tid; q < (K >> 2); q += kStepConsumers) {
+        float4 v = __ldcg(reinterpret_cast<const float4 *>(xcur) + q);
+        for (int p = 0; p < a.tp; p++) {
+            const float4 t = __ldcg(reinterpret_cast<const float4 *>(in + (size_t)p * K) + q);
+            v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+        }
+        reinterpret_cast<float4 *>(xs)[q] = v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    consumers_sync();
+    for (int k = o0 + tid; k < o1; k += kStepConsumers) xnext[k] = xs[k];
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kStepConsumerWarps; i++) tot += red[i];
+    const float sc = 1.0f / sqrtf(tot / (float)K + a.eps);
+    for (int q = tid; q < (K >> 2); q += kStepConsumers) {
+        float4 v = reinterpret_cast<float4 *>(xs)[q];
+        const float4 g = reinterpret_cast<const float4 *>(w)[q];
+        v.x = g.x * v.x * sc; v.y = g.y * v.y * sc; v.z = g.z * v.z * sc; v.w = g.w * v.w * sc;
+        reinterpret_cast<float4 *>(xs)[q] = v;
+    }
+    consumers_sync();
+}
+
+// xs = rmsnorm(src) * w over K elements (src read through L2); with w == nullptr a plain copy.
+// Loads are issued in batches of 4 float4 per thread so that their L2 latencies overlap.
+__device__ __forceinline__ void load_vec(float *xs, const float *src, int K, const float *w, float eps, float *red) {
+    const int tid = threadIdx.x;
+    const int n4 = K >> 2;
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *x4 = reinterpret_cast<float4 *>(xs);
+    float ss = 0.f;
+    for (int b = 0; b < n4; b += 4 * kStepConsumers) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = b + u * kStepConsumers + tid;
+            v[u] = q < n4 ? __ldcg(s4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = b + u * kStepConsumers + tid;
+            if (q < n4) x4[q] = v[u];
+            ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+        }
+    }
+    if (!w) { consumers_sync(); return; }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    consumers_sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kStepConsumerWarps; i++) tot += red[i];
+    const float sc = 1.0f / sqrtf(tot / (float)K + eps);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    for (int q = tid; q < n4; q += kStepConsumers) {
+        float4 v = x4[q];
+        const float4 g = w4[q];
+        v.x = g.x * v.x * sc; v.y = g.y * v.y * sc; v.z = g.z * v.z * sc; v.w = g.w * v.w * sc;
+        x4[q] = v;
+    }
+    consumers_sync();
+}
+
+// xs[p] = up[p] * silu(gate[p]) for the (2F) gate/up outputs, rows interleaved in blocks of 16
+// (kGuBlock) gate rows then the 16 matching up rows; float4-wide, loads batched.
+__device__ __forceinline__ void load_swiglu(float *xs, const float *gu, int F) {
+    const int tid = threadIdx.x;
+    const int n4 = F >> 2;  // float4 outputs
+    float4 *x4 = reinterpret_cast<float4 *>(xs);
+    for (int b = 0; b < n4; b += 4 * kStepConsumers) {
+        float4 g[4], u[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int q = b + k * kStepConsumers + tid;
+            if (q < n4) {
+                const int blk = q >> 2, off = (q & 3) * 4;
+                g[k] = __ldcg(reinterpret_cast<const float4 *>(gu + (size_t)blk * 2 * kGuBlock + off));
+                u[k] = __ldcg(reinterpret_cast<const float4 *>(gu + (size_t)blk * 2 * kGuBlock + kGuBlock + off));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int q = b + k * kStepConsumers + tid;
+            if (q < n4) {
+                float4 h;
+                h.x = u[k].x * (g[k].x * (1.0f / (1.0f + expf(-g[k].x))));
+                h.y = u[k].y * (g[k].y * (1.0f / (1.0f + expf(-g[k].y))));
+                h.z = u[k].z * (g[k].z * (1.0f / (1.0f + expf(-g[k].z))));
+                h.w = u[k].w * (g[k].w * (1.0f / (1.0f + expf(-g[k].w))));
+                x4[q] = h;
+            }
+        }
+    }
+    consumers_sync();
+}
+
+template <typename KT, int DPL> struct SKV;
+template <> struct SKV<__nv_bfloat16, 4> {
+    using T = uint2;
+    static __device__ __forceinline__ T load(const __nv_bfloat16 *p) { return *reinterpret_cast<const uint2 *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) {
+        f[0] = bf16lo(u.x); f[1] = bf16hi(u.x); f[2] = bf16lo(u.y); f[3] = bf16hi(u.y);
+    }
+};
+template <> struct SKV<__nv_bfloat16, 2> {
+    using T = uint32_t;
+    static __device__ __forceinline__ T load(const __nv_bfloat16 *p) { return *reinterpret_cast<const uint32_t *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) { f[0] = bf16lo(u); f[1] = bf16hi(u); }
+};
+template <> struct SKV<float, 4> {
+    using T = float4;
+    static __device__ __forceinline__ T load(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) { f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w; }
+};
+template <> struct SKV<float, 2> {
+    using T = float2;
+    static __device__ __forceinline__ T load(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+    static __device__ __forceinline__ void unpack(const T &u, float *f) { f[0] = u.x; f[1] = u.y; }
+};
+
+// Keys of an attention item's first tile staged into shared memory during the QKV phase.
+template <typename KT>
+__host__ __device__ constexpr int stage_keys() { return sizeof(KT) == 2 ? 64 : 32; }
+
+// Issue cp.async copies of the cached K and V rows [t0, t0 + stage_keys) (except the current
+// position, computed in this step) of KV head kvh into `stage`: K rows, then V rows.
+template <typename KT, int D>
+__device__ __forceinline__ void stage_kv(const StepArgs &a, const StepLayer &Ly, int kvh, int t0, int t1, int pos,
+                                         KT *stage) {
+    constexpr int SK = stage_keys<KT>();
+    constexpr int CH = D * (int)sizeof(KT) / 16;  // 16-byte chunks per row
+    const int nrows = min(SK, t1 - t0);
+    const int *ptab = a.page_table + (size_t)(a.slots ? *a.slots : 0) * a.max_pages;
+    const int ps = a.page_size, lg = a.log2_page;
+    for (int i = threadIdx.x; i < 2 * nrows * CH; i += kStepConsumers) {
+        const int which = i / (nrows * CH), rem = i % (nrows * CH), r = rem / CH, c = rem % CH;
+        const int tt = t0 + r;
+        if (tt == pos) continue;
+        const KT *cache = reinterpret_cast<const KT *>(which ? Ly.vc : Ly.kc);
+        const KT *src = cache + (((size_t)ptab[tt >> lg] * a.Hkv + kvh) * ps + (tt & (ps - 1))) * D + c * (16 / sizeof(KT));
+        const uint32_t dst = su32(stage + (size_t)(which * SK + r) * D) + c * 16;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// One attention work item (KV head kvh, context split sp of ns): QK-norm + RoPE of its query heads
+// and key, the KV-cache write (split 0), online-softmax attention over its keys, partial or final
+// output, and the merge of all splits by the last CTA to finish this KV head.  The whole-vector
+// QK-norm uses the sums of squares the QKV phase accumulated (a.ss).
+template <typename KT, int D, int G>
+__device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int kvh, int sp, int ns, float *sm,
+                          const KT *stage) {
+    constexpr int DPL = D / 32;
+    constexpr int HALF = D / 2;
+    using KV = SKV<KT, DPL>;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float *qs = sm;                 // [G][D]
+    float *ks = qs + G * D;         // [D]
+    float *vs = ks + D;             // [D]
+    float *wo = vs + D;             // [4][G][D]  warp partials, merged in two rounds
+    float *wm = wo + 4 * G * D;     // [8][G]
+    float *wl = wm + 8 * G;         // [8][G]
+    float *mlm = wl + 8 * G;        // [G][64] split maxima, then weights
+    float *mll = mlm + G * 64;      // [G][64] split sums
+    const int pos = *a.positions;
+    const int n = pos + 1;
+    const int chunk = (n + ns - 1) / ns;
+    const int t0 = sp * chunk, t1 = min(n, t0 + chunk);
+    const int Q = a.H * D, KVw = a.Hkv * D;
+    // ---- q heads, k, v of this KV head (one float4 per thread for d 128, G 4) ----
+    float scq = 1.f, sck = 1.f;
+    if (a.qk_mode == 1) {
+        float tq = 0.f, tk = 0.f;
+        if (a.tp > 1) {  // every CTA of every rank added its sums into this rank's accumulator
+            const float *in = reinterpret_cast<const float *>(a.xch[a.rank]) + kXSs + 2 * ((*a.layers_done + layer) & 1);
+            tq = __ldcg(in);
+            tk = __ldcg(in + 1);
+        } else {
+            tq = __ldcg(a.ss + 2 * layer);
+            tk = __ldcg(a.ss + 2 * layer + 1);
+        }
+        scq = 1.0f / sqrtf(tq / (float)a.q_total + 1e-6f);
+        sck = 1.0f / sqrtf(tk / (float)a.kv_total + 1e-6f);
+    }
+    constexpr int NQ4 = G * D / 4, NK4 = D / 4;
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this item's first key tile, staged during the QKV phase
+    for (int i = tid; i < NQ4 + 2 * NK4; i += kStepConsumers) {
+        float4 v;
+        if (i < NQ4) {
+            v = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (size_t)kvh * G * D) + i);
+            if (a.qk_mode == 1) {
+                const float4 g = reinterpret_cast<const float4 *>(Ly.qn + (size_t)kvh * G * D)[i];
+                v.x *= g.x * scq; v.y *= g.y * scq; v.z *= g.z * scq; v.w *= g.w * scq;
+            }
+            reinterpret_cast<float4 *>(qs)[i] = v;
+        } else if (i < NQ4 + NK4) {
+            v = __ldcg(reinterpret_cast<const float4 *>(a.qkv + Q + (size_t)kvh * D) + (i - NQ4));
+            if (a.qk_mode == 1) {
+                const float4 g = reinterpret_cast<const float4 *>(Ly.kn + (size_t)kvh * D)[i - NQ4];
+                v.x *= g.x * sck; v.y *= g.y * sck; v.z *= g.z * sck; v.w *= g.w * sck;
+            }
+            reinterpret_cast<float4 *>(ks)[i - NQ4] = v;
+        } else {
+            v = __ldcg(reinterpret_cast<const float4 *>(a.qkv + Q + KVw + (size_t)kvh * D) + (i - NQ4 - NK4));
+            v.x = Elt<KT>::round(v.x); v.y = Elt<KT>::round(v.y); v.z = Elt<KT>::round(v.z); v.w = Elt<KT>::round(v.w);
+            reinterpret_cast<float4 *>(vs)[i - NQ4 - NK4] = v;
+        }
+    }
+    consumers_sync();
+    if (a.qk_mode == 2) {
+        for (int hh = warp; hh <= G; hh += 8) {
+            float *v = hh < G ? qs + hh * D : ks;
+            const float *w = hh < G ? Ly.qn + (size_t)(kvh * G + hh) * D : Ly.kn + (size_t)kvh * D;
+            float s2 = 0.f;
+            for (int i = lane; i < D; i += 32) s2 += v[i] * v[i];
+            s2 = warp_sum(s2);
+            const float sc = 1.0f / sqrtf(s2 / (float)D + 1e-6f);
+            for (int i = lane; i < D; i += 32) v[i] = w[i] * v[i] * sc;
+        }
+        consumers_sync();
+    }
+    // ---- RoPE (split-half) of the G query heads and the key; the key is rounded to the cache type ----
+    const int *ptab = a.page_table + (size_t)(a.slots ? *a.slots : 0) * a.max_pages;
+    KT *kc = reinterpret_cast<KT *>(Ly.kc);
+    KT *vc = reinterpret_cast<KT *>(Ly.vc);
+    const int ps = a.page_size, lg = a.log2_page, Hkv = a.Hkv;
+    const size_t cbase = (((size_t)ptab[pos >> lg] * Hkv + kvh) * ps + (pos & (ps - 1))) * D;
+    const float2 *fr = a.freq + (size_t)pos * HALF;
+    for (int i = tid; i < (G + 1) * HALF; i += kStepConsumers) {
+        const int hh = i / HALF, f = i % HALF;
+        float *v = hh < G ? qs + hh * D : ks;
+        const float2 cs = fr[f];
+        const float x1 = v[f], x2 = v[f + HALF];
+        float y1 = x1 * cs.x - x2 * cs.y, y2 = x2 * cs.x + x1 * cs.y;
+        if (hh == G) {
+            y1 = Elt<KT>::round(y1);
+            y2 = Elt<KT>::round(y2);
+            if (sp == 0) {
+                Elt<KT>::store(kc + cbase + f, y1);
+                Elt<KT>::store(kc + cbase + f + HALF, y2);
+            }
+        }
+        v[f] = y1;
+        v[f + HALF] = y2;
+    }
+    if (sp == 0)
+        for (int i = tid; i < D; i += kStepConsumers) Elt<KT>::store(vc + cbase + i, vs[i]);
+    consumers_sync();
+    // ---- keys [t0, t1): warp w takes keys t0 + 64 j + 8 w .. + 7 ----
+    float qreg[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int j = 0; j < DPL; j++) qreg[g][j] = qs[g * D + lane * DPL + j] * a.scale;
+    float m[G], l[G], o[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY; l[g] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o[g][j] = 0.f;
+    }
+    for (int tb = t0; tb < t1; tb += 8 * kStepTPW) {
+        typename KV::T kr[kStepTPW], vr[kStepTPW];
+#pragma unroll
+        for (int j = 0; j < kStepTPW; j++) {
+            const int tt = tb + warp * kStepTPW + j;
+            if (tt < t1 && tt != pos) {
+                if (tt < t0 + stage_keys<KT>()) {
+                    kr[j] = KV::load(stage + (size_t)(tt - t0) * D + lane * DPL);
+                    vr[j] = KV::load(stage + (size_t)(stage_keys<KT>() + tt - t0) * D + lane * DPL);
+                } else {
+                    const size_t base = (((size_t)ptab[tt >> lg] * Hkv + kvh) * ps + (tt & (ps - 1))) * D + lane * DPL;
+                    kr[j] = KV::load(kc + base);
+                    vr[j] = KV::load(vc + base);
+                }
+            }
+        }
+        float sc[kStepTPW][G];
+#pragma unroll
+        for (int j = 0; j < kStepTPW; j++) {
+            const int tt = tb + warp * kStepTPW + j;
+            float kf[DPL];
+            if (tt == pos) {
+#pragma unroll
+                for (int e = 0; e < DPL; e++) kf[e] = ks[lane * DPL + e];
+            } else if (tt < t1) {
+                KV::unpack(kr[j], kf);
+            } else {
+#pragma unroll
+                for (int e = 0; e < DPL; e++) kf[e] = 0.f;
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float sdot = 0.f;
+#pragma unroll
+                for (int e = 0; e < DPL; e++) sdot = fmaf(qreg[g][e], kf[e], sdot);
+                sc[j][g] = sdot;
+            }
+        }
+        // reduce the lane-split dot products: the 8 x G sums share the shuffle levels
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int j = 0; j < kStepTPW; j++)
+#pragma unroll
+                for (int g = 0; g < G; g++) sc[j][g] += __shfl_xor_sync(0xffffffffu, sc[j][g], off);
+#pragma unroll
+        for (int j = 0; j < kStepTPW; j++)
+            if (tb + warp * kStepTPW + j >= t1)
+#pragma unroll
+                for (int g = 0; g < G; g++) sc[j][g] = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float mx = m[g];
+#pragma unroll
+            for (int j = 0; j < kStepTPW; j++) mx = fmaxf(mx, sc[j][g]);
+            if (mx == -INFINITY) continue;
+            const float al = expf(m[g] - mx);
+            l[g] *= al;
+#pragma unroll
+            for (int e = 0; e < DPL; e++) o[g][e] *= al;
+            m[g] = mx;
+#pragma unroll
+            for (int j = 0; j < kStepTPW; j++) sc[j][g] = expf(sc[j][g] - mx);
+        }
+#pragma unroll
+        for (int j = 0; j < kStepTPW; j++) {
+            const int tt = tb + warp * kStepTPW + j;
+            if (tt >= t1) continue;
+            float vf[DPL];
+            if (tt == pos) {
+#pragma unroll
+                for (int e = 0; e < DPL; e++) vf[e] = vs[lane * DPL + e];
+            } else {
+                KV::unpack(vr[j], vf);
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                l[g] += sc[j][g];
+#pragma unroll
+                for (int e = 0; e < DPL; e++) o[g][e] = fmaf(sc[j][g], vf[e], o[g][e]);
+            }
+        }
+    }
+    // ---- merge the 8 warps: warps 4..7 into warps 0..3, then the 4 through shared memory ----
+    if (warp >= 4) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            if (lane == 0) { wm[(warp - 4) * G + g] = m[g]; wl[(warp - 4) * G + g] = l[g]; }
+#pragma unroll
+            for (int j = 0; j < DPL; j++) wo[((warp - 4) * G + g) * D + lane * DPL + j] = o[g][j];
+        }
+    }
+    consumers_sync();
+    if (warp < 4) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float om = wm[warp * G + g], ol = wl[warp * G + g];
+            const float M = fmaxf(m[g], om);
+            const float ea = m[g] == -INFINITY ? 0.f : expf(m[g] - M);
+            const float eb = om == -INFINITY ? 0.f : expf(om - M);
+            l[g] = l[g] * ea + ol * eb;
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o[g][j] = o[g][j] * ea + wo[(warp * G + g) * D + lane * DPL + j] * eb;
+            m[g] = M;
+        }
+    }
+    consumers_sync();
+    if (warp < 4) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            if (lane == 0) { wm[warp * G + g] = m[g]; wl[warp * G + g] = l[g]; }
+#pragma unroll
+            for (int j = 0; j < DPL; j++) wo[(warp * G + g) * D + lane * DPL + j] = o[g][j];
+        }
+    }
+    consumers_sync();
+    for (int i = tid; i < G * D; i += kStepConsumers) {
+        const int g = i / D, j = i % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w * G + g]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                const float e = expf(wm[w * G + g] - M);
+                L += wl[w * G + g] * e;
+                O += wo[(w * G + g) * D + j] * e;
+            }
+        }
+        const int h = kvh * G + g;
+        if (ns == 1) {
+            a.attn[(size_t)h * D + j] = O / L;
+        } else {
+            const size_t pidx = (size_t)h * ns + sp;
+            a.part_o[pidx * D + j] = O;
+            if (j == 0) { a.part_ml[pidx * 2] = M; a.part_ml[pidx * 2 + 1] = L; }
+        }
+    }
+    if (ns == 1) return;
+    // ---- every split CTA of this KV head waits for all partials, then merges its slice of the output ----
+    __threadfence();
+    consumers_sync();
+    unsigned *cnt = a.counters + (size_t)layer * a.Hkv + kvh;  // zeroed before the launch
+    if (tid == 0) {
+        atomicAdd(cnt, 1u);
+        const uint64_t w0 = now_ns();
+        while (ld_acquire(cnt) < (unsigned)ns) {
+            if (now_ns() - w0 > kStepWaitNs) { atomicExch(a.err, 3); break; }
+        }
+        __threadfence();
+    }
+    consumers_sync();
+    const int per = (G * D + ns - 1) / ns;
+    const int i0 = sp * per, i1 = min(G * D, i0 + per);
+    // the (max, sum) of every split of the heads this slice touches, and the slice's partial outputs,
+    // loaded in one batch
+    const int g0 = i0 / D, g1 = (i1 - 1) / D;
+    for (int i = tid; i < (g1 - g0 + 1) * ns; i += kStepConsumers) {
+        const int g = g0 + i / ns, sidx = i % ns;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(a.part_ml) + (size_t)(kvh * G + g) * ns + sidx);
+        mlm[g * 64 + sidx] = ml.x;
+        mll[g * 64 + sidx] = ml.y;
+    }
+    // (output, split) pairs of this slice, a few per thread: their partial outputs are loaded in one
+    // batch together with the (max, sum) pairs above, then weighted and summed in shared memory
+    constexpr int kPairs = 5;
+    const int nout = i1 - i0;
+    const int npairs = nout * ns;
+    float *osum = mll + G * 64;  // [per] slice accumulators
+    float pv[kPairs];
+#pragma unroll
+    for (int k = 0; k < kPairs; k++) {
+        const int pi = tid + k * kStepConsumers;
+        pv[k] = 0.f;
+        if (pi < npairs) {
+            const int o = i0 + pi / ns, sidx = pi % ns;
+            pv[k] = __ldcg(a.part_o + ((size_t)(kvh * G + o / D) * ns + sidx) * D + o % D);
+        }
+    }
+    for (int i = tid; i < nout; i += kStepConsumers) osum[i] = 0.f;
+    consumers_sync();  // the (max, sum) pairs are in shared memory
+    if (tid <= g1 - g0) {
+        const int g = g0 + tid;
+        float M = -INFINITY;
+        for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[g * 64 + sidx]);
+        float L = 0.f;
+        for (int sidx = 0; sidx < ns; sidx++) {
+            const float pm = mlm[g * 64 + sidx];
+            const float e = pm == -INFINITY ? 0.f : expf(pm - M);
+            L += mll[g * 64 + sidx] * e;
+            mlm[g * 64 + sidx] = e;
+        }
+        const float inv = 1.0f / L;
+        for (int sidx = 0; sidx < ns; sidx++) mlm[g * 64 + sidx] *= inv;
+    }
+    consumers_sync();
+#pragma unroll
+    for (int k = 0; k < kPairs; k++) {
+        const int pi = tid + k * kStepConsumers;
+        if (pi < npairs) {
+            const int o = i0 + pi / ns, sidx = pi % ns;
+            atomicAdd(osum + (o - i0), mlm[(o / D) * 64 + sidx] * pv[k]);
+        }
+    }
+    for (int pi = tid + kPairs * kStepConsumers; pi < npairs; pi += kStepConsumers) {  // beyond the batch
+        const int o = i0 + pi / ns, sidx = pi % ns;
+        const float v = __ldcg(a.part_o + ((size_t)(kvh * G + o / D) * ns + sidx) * D + o % D);
+        atomicAdd(osum + (o - i0), mlm[(o / D) * 64 + sidx] * v);
+    }
+    consumers_sync();
+    for (int i = tid; i < nout; i += kStepConsumers) a.attn[(size_t)kvh * G * D + i0 + i] = osum[i];
+}
+
+template <typename KT, int D, int G, bool TPM>
+__global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bar[kRing], empty_bar[kRing];
+    __shared__ int abort_sh;
+    __shared__ float red[kStepConsumerWarps], red2[kStepConsumerWarps];
+    __shared__ float am_v[kStepConsumers];
+    __shared__ int am_i[kStepConsumers];
+    uint8_t *ring = smem;                                            // kRing * kPiece
+    float *xs = reinterpret_cast<float *>(smem + kRing * kPiece);    // max K floats
+    float *acc = xs + a.xs_floats;                                   // max rows per CTA
+    float *scratch = xs;                                             // attention phase only
+    KT *stage = reinterpret_cast<KT *>(xs + a.stage_off);            // staged keys of this CTA's attention item
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int *abort_flag = &abort_sh;
+    if (tid == 0) {
+        for (int i = 0; i < kRing; i++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full_bar[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&empty_bar[i])), "r"(kStepConsumerWarps)
+                         : "memory");
+        }
+        abort_sh = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    Ring rg{full_bar, empty_bar, ring, 0, 0u};
+    const int D_ = a.D, Q = a.H * D, KVw = a.Hkv * D, QKV = Q + 2 * KVw, F = a.F;
+
+    if (warp == kStepConsumerWarps) {
+        // ======================= producer =======================
+        if (lane == 0) {
+            uint32_t issued = 0, last_ph = 0;
+            bool ok = true;
+            for (int l = 0; l < a.layers && ok; l++) {
+                const StepLayer &Ly = a.L[l];
+                ok = ok && produce(rg, Ly.w_qkv, QKV, D_, abort_flag, a.err, issued, last_ph);
+                ok = ok && produce(rg, Ly.w_o, D_, Q, abort_flag, a.err, issued, last_ph);
+                ok = ok && produce(rg, Ly.w_gu, 2 * F, D_, abort_flag, a.err, issued, last_ph);
+                ok = ok && produce(rg, Ly.w_down, D_, F, abort_flag, a.err, issued, last_ph);
+            }
+            ok = ok && produce(rg, a.lm, a.V, D_, abort_flag, a.err, issued, last_ph);
+            if (!ok) {
+                for (int i = 0; i < kRing; i++)
+                    if (issued >> i & 1u) {
+                        const uint32_t addr = su32(&full_bar[i]);
+                        const uint64_t t0 = now_ns();
+                        while (!mb_try(addr, (last_ph >> i) & 1u) && now_ns() - t0 < kStepWaitNs) {
+                        }
+                    }
+            }
+        }
+        return;
+    }
+
+    // ======================= consumers =======================
+    unsigned target = 0;
+    unsigned gen = TPM ? *a.gen : 0u;                 // cross-rank barriers passed (monotonic across steps)
+    const unsigned lbase = TPM ? *a.layers_done : 0u;  // layers run by earlier steps (QK-norm sum slots alternate)
+    int r0, r1;
+    const int token = *a.tokens;
+    constexpr bool tpm = TPM;  // tensor parallel: compiled only into the tp > 1 variants
+    const int box_o = kXRows, box_d = kXRows + a.tp * D_;
+    float *xcur = a.x, *xnext = a.x2;  // residual stream (ping-pong under tensor parallelism)
+    if (a.trace && blockIdx.x == 0 && tid == 0) a.trace[0] = trace_ns();
+    for (int l = 0; l < a.layers; l++) {
+        const StepLayer &Ly = a.L[l];
+        // ---- rmsnorm + QKV ----
+        if (l == 0) {
+            const __nv_bfloat16 *er = a.embed + (size_t)token * D_;
+            for (int k = tid; k < D_; k += kStepConsumers) {
+                const float v = __bfloat162float(er[k]);
+                if (blockIdx.x == 0) xcur[k] = v;
+                xs[k] = v;
+            }
+            consumers_sync();
+            // normalise in place (load_vec reads through L2; here the row came from the table)
+            float ss = 0.f;
+            for (int k = tid; k < D_; k += kStepConsumers) ss += xs[k] * xs[k];
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            consumers_sync();
+            float tot = 0.f;
+            for (int i = 0; i < kStepConsumerWarps; i++) tot += red[i];
+            const float sc = 1.0f / sqrtf(tot / (float)D_ + a.eps);
+            for (int k = tid; k < D_; k += kStepConsumers) xs[k] = Ly.rms_att[k] * xs[k] * sc;
+            consumers_sync();
+        } else if (tpm) {
+            load_resid(a, xs, xcur, box_d, xnext, Ly.rms_att, red);
+            float *t = xcur; xcur = xnext; xnext = t;
+        } else {
+            load_vec(xs, xcur, D_, Ly.rms_att, a.eps, red);
+        }
+        {
+            // start fetching this CTA's attention keys now: they land behind the QKV weight stream
+            const int n = *a.positions + 1;
+            const int ns = attn_splits(gridDim.x, a.Hkv, n);
+            if ((int)blockIdx.x < a.Hkv * ns) {
+                const int kvh = blockIdx.x / ns, sp = blockIdx.x % ns;
+                const int chunk = (n + ns - 1) / ns;
+                const int t0 = sp * chunk, t1 = min(n, t0 + chunk);
+                if (t0 < t1) stage_kv<KT, D>(a, Ly, kvh, t0, t1, n - 1, stage);
+            }
+        }
+        if (!consume(rg, QKV, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
+        {
+            // the QKV rows, and the sums of squares of the q and k rows for the whole-vector QK-norm
+            float sq = 0.f, sk = 0.f;
+            for (int r = tid; r < r1 - r0; r += kStepConsumers) {
+                const float v = acc[r] + (Ly.b_qkv ? Ly.b_qkv[r0 + r] : 0.f);
+                a.qkv[r0 + r] = v;
+                if (r0 + r < Q) sq += v * v;
+                else if (r0 + r < Q + KVw) sk += v * v;
+            }
+            if (a.qk_mode == 1) {
+                sq = warp_sum(sq);
+                sk = warp_sum(sk);
+                if (lane == 0) { red[warp] = sq; red2[warp] = sk; }
+                consumers_sync();
+                float tq = 0.f, tk = 0.f;
+                for (int w = 0; w < kStepConsumerWarps; w++) { tq += red[w]; tk += red2[w]; }
+                sq = tq;
+                sk = tk;
+                if (tid == 0 && !tpm) {
+                    if (tq != 0.f) atomicAdd(a.ss + 2 * l, tq);
+                    if (tk != 0.f) atomicAdd(a.ss + 2 * l + 1, tk);
+                }
+            }
+            if (tpm && a.qk_mode == 1) {
+                // the accumulator slot the next layer uses was last read two layers ago: clear it now
+                // (slots alternate by the global layer count, which continues across steps)
+                if (blockIdx.x == 0 && tid == 0) {
+                    float *nxt = reinterpret_cast<float *>(a.xch[a.rank]) + kXSs + 2 * ((lbase + l + 1) & 1);
+                    nxt[0] = 0.f;
+                    nxt[1] = 0.f;
+                }
+                if (!cross_sync(a, target, gen, PUB_SS, lbase + l, sq, sk, abort_flag)) break;
+            } else if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) {
+                break;
+            }
+        }
+        // ---- attention (this rank's heads) ----
+        {
+            const int n = *a.positions + 1;
+            const int ns = attn_splits(gridDim.x, a.Hkv, n);
+            if ((int)blockIdx.x < a.Hkv * ns)
+                attn_item<KT, D, G>(a, Ly, l, blockIdx.x / ns, blockIdx.x % ns, ns, scratch, stage);
+        }
+        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        // ---- O projection + residual (summed over ranks through the inboxes) ----
+        load_vec(xs, a.attn, Q, nullptr, 0.f, red);
+        if (!consume(rg, D_, Q, xs, acc, r0, r1, abort_flag, a.err)) break;
+        if (tpm) {
+            push_partial(a, box_o, r0, r1, acc);
+            if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
+            load_resid(a, xs, xcur, box_o, xnext, Ly.rms_ffn, red);
+            float *t = xcur; xcur = xnext; xnext = t;
+        } else {
+            for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
+            if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+            load_vec(xs, xcur, D_, Ly.rms_ffn, a.eps, red);
+        }
+        // ---- gate/up (raw) ----
+        if (!consume(rg, 2 * F, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
+        for (int r = tid; r < r1 - r0; r += kStepConsumers) a.gu[r0 + r] = acc[r];
+        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        // ---- SwiGLU (rows interleaved 16 gate / 16 up) + down + residual ----
+        load_swiglu(xs, a.gu, F);
+        if (!consume(rg, D_, F, xs, acc, r0, r1, abort_flag, a.err)) break;
+        if (tpm) {
+            push_partial(a, box_d, r0, r1, acc);
+            if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
+        } else {
+            for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
+            if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        }
+    }
+    if (*abort_flag) return;
+    // ---- final rmsnorm + lm_head (this rank's vocabulary rows) + argmax ----
+    if (tpm) load_resid(a, xs, xcur, box_d, xnext, a.norm_final, red);
+    else load_vec(xs, xcur, D_, a.norm_final, a.eps, red);
+    if (!consume(rg, a.V, D_, xs, acc, r0, r1, abort_flag, a.err)) return;
+    if (a.trace && blockIdx.x == 0 && tid == 0) a.trace[2 * (target / gridDim.x) + 1] = trace_ns();
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int r = tid; r < r1 - r0; r += kStepConsumers) {
+        const float v = acc[r];
+        if (a.logits) a.logits[r0 + r] = v;
+        if (v > bv) { bv = v; bi = r0 + r; }
+    }
+    am_v[tid] = bv;
+    am_i[tid] = bi;
+    consumers_sync();
+    if (tid < 32) {
+        for (int i = tid + 32; i < kStepConsumers; i += 32)
+            if (am_v[i] > bv || (am_v[i] == bv && am_i[i] < bi)) { bv = am_v[i]; bi = am_i[i]; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (tid == 0) {
+            a.am_val[blockIdx.x] = bv;
+            a.am_idx[blockIdx.x] = bi + a.v0;
+            __threadfence();
+            atomicAdd(a.bar, 1u);
+        }
+    }
+    // CTA 0 gathers every CTA's winner, then (tensor parallel) every rank's, and feeds the token back
+    if (blockIdx.x != 0 || warp != 0) return;
+    target += gridDim.x;
+    bool ok = true;
+    if (lane == 0) {
+        const uint64_t t0 = now_ns();
+        while (ld_acquire(a.bar) < target)
+            if (now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    __threadfence();
+    bv = -FLT_MAX;
+    bi = INT_MAX;
+    for (int c = lane; c < (int)gridDim.x; c += 32) {
+        const float v = __ldcg(a.am_val + c);
+        const int i = __ldcg(a.am_idx + c);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (tpm) {
+        // one more flat barrier in which only CTA 0 of each rank takes part: its counter slot grows
+        // by gridDim.x so that the counters stay multiples of the grid
+        gen += 1u;
+        if (lane == 0 && ok) {
+            for (int p = 0; p < a.tp; p++) {
+                unsigned *in = a.xch[p] + kXAm + 2 * a.rank;
+                in[0] = __float_as_uint(bv);
+                in[1] = (unsigned)bi;
+            }
+            __threadfence_system();
+            for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, gridDim.x);
+            const unsigned want = gen * gridDim.x;
+            const unsigned *mine = a.xch[a.rank] + kXFlags;
+            const uint64_t t0 = now_ns();
+            for (int p = 0; ok && p < a.tp; p++)
+                while ((int)(ld_acquire_sys(mine + p) - want) < 0)
+                    if (now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        bv = -FLT_MAX;
+        bi = INT_MAX;
+        if (lane < a.tp) {
+            const unsigned *in = a.xch[a.rank] + kXAm + 2 * lane;
+            bv = __uint_as_float(__ldcg(in));
+            bi = (int)__ldcg(in + 1);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+    }
+    if (lane == 0) {
+        if (!ok) {
+            atomicExch(a.err, 5);
+            return;
+        }
+        if (a.argmax_out) *a.argmax_out = bi;
+        if (a.hist) a.hist[*a.positions + 1] = bi;
+        if (a.advance) {
+            *a.tokens = bi;
+            *a.positions += 1;
+        }
+        if (TPM) {
+            *a.gen = gen;
+            *a.layers_done = lbase + a.layers;
+        }
+    }
+}
+
+template <typename KT, int D, bool TPM>
+const void *step_fn_g(int G) {
+    switch (G) {
+        case 1: return (const void *)step_kernel<KT, D, 1, TPM>;
+        case 2: return (const void *)step_kernel<KT, D, 2, TPM>;
+        case 4: return (const void *)step_kernel<KT, D, 4, TPM>;
+        case 8: return (const void *)step_kernel<KT, D, 8, TPM>;
+    }
+    return nullptr;
+}
+
+}  // namespace
+}  // namespace qw
