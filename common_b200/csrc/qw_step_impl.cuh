@@ -94,10 +94,11 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
 template <typename T>
 __device__ __forceinline__ T ldcg(const T *p) { return __ldcg(p); }
 
-// context splits of the attention phase: at most one work item per CTA, at least 16 keys per split
+// context splits of the attention phase: at most one work item per CTA, at least 16 keys per split,
+// at most 16 splits
 __device__ __forceinline__ int attn_splits(int grid, int Hkv, int n) {
     int ns = min(grid / Hkv, (n + 15) / 16);
-    return max(1, min(ns, 64));
+    return max(1, min(ns, 16));  // <= 16: the split merge loads every partial in one round
 }
 
 __device__ __forceinline__ void split_rows(int N, int c, int n, int &r0, int &r1) {
@@ -806,54 +807,49 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         mlm[g * 64 + sidx] = ml.x;
         mll[g * 64 + sidx] = ml.y;
     }
-    // (output, split) pairs of this slice, a few per thread: their partial outputs are loaded in one
-    // batch together with the (max, sum) pairs above, then weighted and summed in shared memory
-    constexpr int kPairs = 5;
-    const int nout = i1 - i0;
-    const int npairs = nout * ns;
-    float *osum = mll + G * 64;  // [per] slice accumulators
-    float pv[kPairs];
+    constexpr int kMaxPV = 16;  // = the most splits attn_splits makes: one round of loads
+    // outputs in rounds of one per thread; a round's loads of every split are issued together
+    const int rounds = (i1 - i0 + kStepConsumers - 1) / kStepConsumers;
+    float pv[kMaxPV];
+    for (int rd = 0; rd < rounds; rd++) {
+        const int oi = i0 + rd * kStepConsumers + tid;
+        const bool mine = oi < i1;
+        if (mine && ns <= kMaxPV) {
+            const float *po = a.part_o + (size_t)(kvh * G + oi / D) * ns * D + oi % D;
 #pragma unroll
-    for (int k = 0; k < kPairs; k++) {
-        const int pi = tid + k * kStepConsumers;
-        pv[k] = 0.f;
-        if (pi < npairs) {
-            const int o = i0 + pi / ns, sidx = pi % ns;
-            pv[k] = __ldcg(a.part_o + ((size_t)(kvh * G + o / D) * ns + sidx) * D + o % D);
+            for (int sidx = 0; sidx < kMaxPV; sidx++) pv[sidx] = sidx < ns ? __ldcg(po + (size_t)sidx * D) : 0.f;
         }
-    }
-    for (int i = tid; i < nout; i += kStepConsumers) osum[i] = 0.f;
-    consumers_sync();  // the (max, sum) pairs are in shared memory
-    if (tid <= g1 - g0) {
-        const int g = g0 + tid;
-        float M = -INFINITY;
-        for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[g * 64 + sidx]);
-        float L = 0.f;
-        for (int sidx = 0; sidx < ns; sidx++) {
-            const float pm = mlm[g * 64 + sidx];
-            const float e = pm == -INFINITY ? 0.f : expf(pm - M);
-            L += mll[g * 64 + sidx] * e;
-            mlm[g * 64 + sidx] = e;
+        if (rd == 0) {
+            consumers_sync();  // the (max, sum) loads above are in shared memory
+            if (tid <= g1 - g0) {
+                const int g = g0 + tid;
+                float M = -INFINITY;
+                for (int sidx = 0; sidx < ns; sidx++) M = fmaxf(M, mlm[g * 64 + sidx]);
+                float L = 0.f;
+                for (int sidx = 0; sidx < ns; sidx++) {
+                    const float pm = mlm[g * 64 + sidx];
+                    const float e = pm == -INFINITY ? 0.f : expf(pm - M);
+                    L += mll[g * 64 + sidx] * e;
+                    mlm[g * 64 + sidx] = e;
+                }
+                const float inv = 1.0f / L;
+                for (int sidx = 0; sidx < ns; sidx++) mlm[g * 64 + sidx] *= inv;
+            }
+            consumers_sync();
         }
-        const float inv = 1.0f / L;
-        for (int sidx = 0; sidx < ns; sidx++) mlm[g * 64 + sidx] *= inv;
-    }
-    consumers_sync();
+        if (!mine) continue;
+        const int g = oi / D;
+        float O = 0.f;
+        if (ns <= kMaxPV) {
 #pragma unroll
-    for (int k = 0; k < kPairs; k++) {
-        const int pi = tid + k * kStepConsumers;
-        if (pi < npairs) {
-            const int o = i0 + pi / ns, sidx = pi % ns;
-            atomicAdd(osum + (o - i0), mlm[(o / D) * 64 + sidx] * pv[k]);
+            for (int sidx = 0; sidx < kMaxPV; sidx++)
+                if (sidx < ns) O += mlm[g * 64 + sidx] * pv[sidx];
+        } else {
+            const float *po = a.part_o + (size_t)(kvh * G + g) * ns * D + oi % D;
+            for (int sidx = 0; sidx < ns; sidx++) O += mlm[g * 64 + sidx] * __ldcg(po + (size_t)sidx * D);
         }
+        a.attn[(size_t)kvh * G * D + oi] = O;
     }
-    for (int pi = tid + kPairs * kStepConsumers; pi < npairs; pi += kStepConsumers) {  // beyond the batch
-        const int o = i0 + pi / ns, sidx = pi % ns;
-        const float v = __ldcg(a.part_o + ((size_t)(kvh * G + o / D) * ns + sidx) * D + o % D);
-        atomicAdd(osum + (o - i0), mlm[(o / D) * 64 + sidx] * v);
-    }
-    consumers_sync();
-    for (int i = tid; i < nout; i += kStepConsumers) a.attn[(size_t)kvh * G * D + i0 + i] = osum[i];
 }
 
 template <typename KT, int D, int G, bool TPM>
