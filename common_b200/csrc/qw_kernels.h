@@ -111,6 +111,25 @@ struct RowsArgmaxArgs {
     int hist_ld;
 };
 
+struct SampleArgs {
+    const float *logits;  // (rows, ld)
+    int ld, V;
+    double temperature;   // <= 0: greedy
+    double top_p;         // mode 1 only; >= 1: no nucleus filter
+    int mode;             // 0: the Qwen3 generation sampler (softmax, then sampleToken's second softmax); 1: sampleToken
+    const double *r;      // (rows) uniform draws, or nullptr: draw from rng
+    unsigned long long *rng;  // (rows) java.util.Random states
+    double *scratch;      // (rows, V)
+    int *out;             // (rows) nullable
+    int *next_tokens, *positions;  // advance: next_tokens[row] = token, positions[row] += 1
+    int advance;
+    int *hist;
+    int hist_ld;
+};
+
+cudaError_t sample_rows_launch(const SampleArgs &a, int rows, cudaStream_t st);
+unsigned long long java_random_state(long long seed);
+
 cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st);
 cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st);
 cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st);

@@ -92,6 +92,11 @@ struct qw_model {
     std::vector<void *> xch_peer;           // peers' exchange buffers opened through CUDA IPC
     unsigned **d_xch = nullptr;             // device array of all ranks' exchange buffers
     unsigned *d_persist = nullptr;          // barrier generation + release word, persistent
+    // sampling (qw_set_sampling): temperature <= 0 keeps greedy decoding
+    double samp_temperature = 0.0, samp_top_p = 1.0;
+    int samp_mode = 0;
+    unsigned long long *d_rng = nullptr;    // (B) java.util.Random states
+    double *d_samp = nullptr;               // (B, V) probabilities
     // graph
     cudaGraphExec_t graph = nullptr;
     int launches = 0;
@@ -742,6 +747,21 @@ qw_status tc_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, i
     return QW_OK;
 }
 
+// (B, V) device logits of a step: the rank's own buffer at tp 1, the gathered block otherwise
+float *full_logits(qw_model *m) { return m->logits_all ? m->logits_all + (size_t)m->tp * m->B * m->Vl : m->logits; }
+
+// draw the next token of rows 0..batch-1 from (batch, V) logits with the model's sampling settings
+qw_status sample_launch(qw_model *m, const float *logits, int batch, int *out, int advance, int *next_tokens,
+                        int *positions, int *hist, int hist_ld) {
+    SampleArgs a{};
+    a.logits = logits; a.ld = m->c.vocab; a.V = m->c.vocab;
+    a.temperature = m->samp_temperature; a.top_p = m->samp_top_p; a.mode = m->samp_mode;
+    a.r = nullptr; a.rng = m->d_rng; a.scratch = m->d_samp; a.out = out;
+    a.advance = advance; a.next_tokens = next_tokens; a.positions = positions; a.hist = hist; a.hist_ld = hist_ld;
+    LK(sample_rows_launch(a, batch, m->st));
+    return QW_OK;
+}
+
 }  // namespace
 
 // ==========================================================================================
@@ -1158,6 +1178,47 @@ qw_status qw_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, i
     return QW_OK;
 }
 
+// Sampled generation (AutoregressiveModel.next with a temperature): the prompt's last logits give the
+// first generated token; every later step writes its logits and the sampling kernel feeds the drawn token
+// back and advances the position, all on the device.
+static qw_status generate_sampled(qw_model *m, const int32_t *prompts, int32_t batch, int32_t prompt_len,
+                                  int32_t steps, int32_t *tokens_out) {
+    const int V = m->c.vocab;
+    std::vector<float> lg((size_t)batch * V);
+    for (int b = 0; b < batch; b++) release_slot(m, b);
+    for (int b = 0; b < batch; b++) {
+        qw_status s = reserve_pages(m, b, steps);
+        if (s) return s;
+    }
+    qw_status s = qw_prefill(m, prompts, nullptr, batch, prompt_len, lg.data(), nullptr);
+    if (s) return s;
+    for (int b = 0; b < batch; b++)
+        for (int i = 0; i < prompt_len; i++) tokens_out[(size_t)b * steps + i] = prompts[(size_t)b * prompt_len + i];
+    if (steps == prompt_len) return QW_OK;
+    float *dlog = full_logits(m);
+    int *hist = nullptr;
+    AL(hist, (size_t)batch * (steps + 1));
+    std::vector<int> pos(batch, prompt_len - 1);
+    CK(cudaMemcpyAsync(dlog, lg.data(), sizeof(float) * lg.size(), cudaMemcpyHostToDevice, m->st));
+    CK(cudaMemcpyAsync(m->d_pos, pos.data(), sizeof(int) * batch, cudaMemcpyHostToDevice, m->st));
+    // the first generated token: its position is prompt_len (the draw advances d_pos to it)
+    s = sample_launch(m, dlog, batch, nullptr, 1, m->d_tokens, m->d_pos, hist, steps + 1);
+    for (int st = prompt_len; !s && st < steps - 1; st++) {
+        s = device_step(m, m->d_tokens, nullptr, m->d_slots, m->d_pos, batch, dlog, m->d_argmax, 0, nullptr, 0);
+        if (!s) s = sample_launch(m, dlog, batch, nullptr, 1, m->d_tokens, m->d_pos, hist, steps + 1);
+    }
+    std::vector<int> h((size_t)batch * (steps + 1));
+    cudaError_t e = cudaSuccess;
+    if (!s) e = cudaMemcpyAsync(h.data(), hist, sizeof(int) * h.size(), cudaMemcpyDeviceToHost, m->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->st);
+    cudaFree(hist);
+    if (s) return s;
+    if (e != cudaSuccess) return fail(m, QW_ERR_CUDA, "generate: %s", cudaGetErrorString(e));
+    for (int b = 0; b < batch; b++)
+        for (int i = prompt_len; i < steps; i++) tokens_out[(size_t)b * steps + i] = h[(size_t)b * (steps + 1) + i];
+    return QW_OK;
+}
+
 qw_status qw_generate(qw_model *m, const int32_t *prompts, int32_t batch, int32_t prompt_len, int32_t steps,
                       int32_t *tokens_out) {
     if (!m) return QW_ERR_ARG;
@@ -1177,6 +1238,7 @@ qw_status qw_generate(qw_model *m, const int32_t *prompts, int32_t batch, int32_
     for (int b = 0; b < batch; b++)
         for (int i = 0; i < prompt_len; i++) tokens_out[(size_t)b * steps + i] = prompts[(size_t)b * prompt_len + i];
     if (steps == prompt_len) return QW_OK;
+    if (m->samp_temperature > 0.0) return generate_sampled(m, prompts, batch, prompt_len, steps, tokens_out);
     // device-resident greedy loop: the argmax epilogue feeds the next step and advances positions
     int *hist = nullptr;
     AL(hist, (size_t)batch * (steps + 1));
@@ -1262,6 +1324,57 @@ qw_status qw_set_device_inputs(qw_model *m, const int32_t *tokens, const int32_t
     return QW_OK;
 }
 
+qw_status qw_set_sampling(qw_model *m, double temperature, double top_p, int64_t seed, int32_t mode) {
+    if (!m) return QW_ERR_ARG;
+    if (mode != 0 && mode != 1) return fail(m, QW_ERR_ARG, "sampling mode %d (0 or 1)", mode);
+    if (!(top_p > 0.0)) return fail(m, QW_ERR_ARG, "top_p must be positive");
+    CK(cudaSetDevice(m->dev));
+    if (!m->d_rng) {
+        AL(m->d_rng, m->B);
+        AL(m->d_samp, (size_t)m->B * m->c.vocab);
+    }
+    std::vector<unsigned long long> st(m->B);
+    for (int b = 0; b < m->B; b++) st[b] = java_random_state(seed + b);  // new Random(seed + slot)
+    CK(cudaMemcpy(m->d_rng, st.data(), sizeof(unsigned long long) * m->B, cudaMemcpyHostToDevice));
+    m->samp_temperature = temperature;
+    m->samp_top_p = top_p;
+    m->samp_mode = mode;
+    return QW_OK;
+}
+
+qw_status qw_decode_sample(qw_model *m, const int32_t *tokens, const int32_t *slots, const int32_t *positions,
+                           int32_t batch, int32_t *tokens_out) {
+    if (!m) return QW_ERR_ARG;
+    if (!tokens || !positions || !tokens_out) return fail(m, QW_ERR_ARG, "null argument");
+    if (!m->finalized) return fail(m, QW_ERR_STATE, "weights not finalized");
+    if (batch < 1 || batch > m->B) return fail(m, QW_ERR_SHAPE, "batch %d outside [1,%d]", batch, m->B);
+    if (m->samp_temperature > 0.0 && !m->d_rng) return fail(m, QW_ERR_STATE, "sampling state not set");
+    CK(cudaSetDevice(m->dev));
+    for (int b = 0; b < batch; b++)
+        if (tokens[b] < 0 || tokens[b] >= m->c.vocab) return fail(m, QW_ERR_ARG, "token %d outside vocab", tokens[b]);
+    qw_status s = check_positions(m, slots, positions, batch);
+    if (s) return s;
+    int *pin = m->h_pin_i;
+    const int MB = m->B;
+    memcpy(pin, tokens, sizeof(int) * batch);
+    memcpy(pin + MB, positions, sizeof(int) * batch);
+    if (slots) memcpy(pin + 2 * MB, slots, sizeof(int) * batch);
+    else for (int b = 0; b < batch; b++) pin[2 * MB + b] = b;
+    CK(cudaMemcpyAsync(m->d_tokens, pin, sizeof(int) * 3 * MB, cudaMemcpyHostToDevice, m->st));
+    float *dlog = full_logits(m);
+    if (m->samp_temperature > 0.0) {
+        s = device_step(m, m->d_tokens, nullptr, m->d_tokens + 2 * MB, m->d_pos, batch, dlog, m->d_argmax, 0, nullptr, 0);
+        if (!s) s = sample_launch(m, dlog, batch, m->d_argmax, 0, nullptr, nullptr, nullptr, 0);
+    } else {
+        s = device_step(m, m->d_tokens, nullptr, m->d_tokens + 2 * MB, m->d_pos, batch, nullptr, m->d_argmax, 0, nullptr, 0);
+    }
+    if (s) return s;
+    CK(cudaMemcpyAsync(pin + 3 * MB, m->d_argmax, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    memcpy(tokens_out, pin + 3 * MB, sizeof(int) * batch);
+    return QW_OK;
+}
+
 qw_status qw_synchronize(qw_model *m) {
     if (!m) return QW_ERR_ARG;
     CK(cudaSetDevice(m->dev));
@@ -1301,6 +1414,7 @@ void qw_destroy(qw_model *m) {
     for (void *q : m->xch_peer)
         if (q) cudaIpcCloseMemHandle(q);
     cudaFree(m->xch); cudaFree(m->d_xch); cudaFree(m->d_persist);
+    cudaFree(m->d_rng); cudaFree(m->d_samp);
     if (m->h_pin_i) cudaFreeHost(m->h_pin_i);
     prefill_free(m->pf);
     if (m->comm) ncclCommDestroy(m->comm);

@@ -122,3 +122,19 @@ extern "C" qw_status qw_op_linear(const void *w, int32_t n_out, int32_t k, const
     if (e != cudaSuccess) return op_fail(QW_ERR_CUDA, std::string("linear launch: ") + cudaGetErrorString(e));
     return QW_OK;
 }
+
+extern "C" qw_status qw_op_sample(const float *logits, int32_t rows, int32_t vocab, int32_t ld, double temperature,
+                                  double top_p, int32_t mode, const double *r_uniform, double *scratch,
+                                  int32_t *tokens_out, void *stream) {
+    if (!logits || !tokens_out || (temperature > 0.0 && (!r_uniform || !scratch)))
+        return op_fail(QW_ERR_ARG, "null device pointer");
+    if (rows < 1 || vocab < 1 || ld < vocab) return op_fail(QW_ERR_SHAPE, "rows, vocab >= 1 and ld >= vocab");
+    if (mode != 0 && mode != 1) return op_fail(QW_ERR_ARG, "mode 0 or 1");
+    if (!(top_p > 0.0)) return op_fail(QW_ERR_ARG, "top_p must be positive");
+    SampleArgs a{};
+    a.logits = logits; a.ld = ld; a.V = vocab; a.temperature = temperature; a.top_p = top_p; a.mode = mode;
+    a.r = r_uniform; a.scratch = scratch; a.out = tokens_out;
+    cudaError_t e = sample_rows_launch(a, rows, (cudaStream_t)stream);
+    if (e != cudaSuccess) return op_fail(QW_ERR_CUDA, std::string("sample launch: ") + cudaGetErrorString(e));
+    return QW_OK;
+}

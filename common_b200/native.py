@@ -25,7 +25,7 @@ EXPORTS = ("qw_abi_version", "qw_build_info", "qw_get_unique_id", "qw_create", "
            "qw_finalize_weights", "qw_reset", "qw_reserve", "qw_decode_step", "qw_forward_hidden", "qw_prefill",
            "qw_generate", "qw_decode_step_device", "qw_capture_decode", "qw_replay_decode", "qw_synchronize",
            "qw_stream", "qw_last_launch_count", "qw_last_error", "qw_destroy", "qw_profile_decode",
-           "qw_set_device_inputs", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static", "qw_op_linear")
+           "qw_set_device_inputs", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static", "qw_op_linear", "qw_set_sampling", "qw_decode_sample", "qw_op_sample")
 KERNEL_NAMES = {0: "other", 1: "qkv", 2: "attn", 3: "o_proj", 4: "gate_up", 5: "down", 6: "lm_head", 7: "step"}
 
 
@@ -83,6 +83,9 @@ def load() -> C.CDLL:
         "qw_profile_decode": (I32, [P, I32, PF, PI, I32, PI]),
         "qw_set_device_inputs": (I32, [P, PI, PI, I32]),
         "qw_op_lm_head_argmax": (I32, [P, I32, I32, I32, P, P, C.c_double, I32, P, P, P]),
+        "qw_set_sampling": (I32, [P, C.c_double, C.c_double, C.c_int64, I32]),
+        "qw_decode_sample": (I32, [P, PI, PI, PI, I32, PI]),
+        "qw_op_sample": (I32, [P, I32, I32, I32, C.c_double, C.c_double, I32, P, P, P, P]),
         "qw_op_linear": (I32, [P, I32, I32, P, I32, I32, P, P, P, P]),
         "qw_op_lm_head_argmax_static": (I32, [P, I32, I32, I32, P, P, C.c_double, I32, P, P, P]),
     }
@@ -124,6 +127,15 @@ def op_lm_head_argmax(w_ptr: int, w_dtype: int, vocab: int, dim: int, x_ptr: int
     """qw_op_lm_head_argmax over raw device pointers."""
     st = load().qw_op_lm_head_argmax(w_ptr, w_dtype, vocab, dim, x_ptr, norm_ptr, eps, batch, logits_ptr or None,
                                      argmax_ptr, stream or None)
+    if st:
+        raise QwenError(st, op_error())
+
+
+def op_sample(logits_ptr: int, rows: int, vocab: int, ld: int, temperature: float, top_p: float, mode: int,
+              r_ptr: int, scratch_ptr: int, out_ptr: int, stream: int = 0) -> None:
+    """qw_op_sample over raw device pointers."""
+    st = load().qw_op_sample(logits_ptr, rows, vocab, ld, temperature, top_p, mode, r_ptr or None,
+                             scratch_ptr or None, out_ptr, stream or None)
     if st:
         raise QwenError(st, op_error())
 
@@ -241,6 +253,17 @@ class NativeModel:
         am = np.zeros(B, np.int32)
         self._check(self.L.qw_prefill(self.h, _ip(t), _ip(s), B, S, _fp(logits), _ip(am)))
         return logits, am
+
+    def set_sampling(self, temperature: float, top_p: float = 1.0, seed: int = 0, mode: int = 0):
+        self._check(self.L.qw_set_sampling(self.h, temperature, top_p, seed, mode))
+
+    def decode_sample(self, tokens, positions, slots=None):
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        s = None if slots is None else np.ascontiguousarray(slots, np.int32)
+        out = np.zeros(t.size, np.int32)
+        self._check(self.L.qw_decode_sample(self.h, _ip(t), _ip(s), _ip(p), t.size, _ip(out)))
+        return out
 
     def generate(self, prompts, steps: int):
         p = np.ascontiguousarray(prompts, np.int32)

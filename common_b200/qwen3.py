@@ -156,7 +156,9 @@ class CompiledModel:
 
 
 class AutoregressiveModel:
-    """Greedy (temperature 0) generation loop of AutoregressiveModel.next()."""
+    """The generation loop of AutoregressiveModel.next() (AutoregressiveModel.java:295-308): prompt tokens are
+    fed first, then each step samples from the previous step's output -- greedily at temperature 0, else with
+    the sampler Qwen3 builds in AutoregressiveModel.of (:405-434), drawn on the device."""
 
     def __init__(self, owner: "Qwen3"):
         self._o = owner
@@ -183,10 +185,16 @@ class AutoregressiveModel:
     def getCurrentStep(self) -> int:
         return self.currentStep
 
-    def setTemperature(self, t: float):
-        if t != 0.0:
-            raise ValueError("only greedy decoding (temperature 0) is implemented on the device path")
-        self.temperature = t
+    def setTemperature(self, t: float, seed: int | None = None):
+        """AutoregressiveModel.setTemperature (:59-61).  The reference draws from an unseeded java.util.Random;
+        here the draws come from java.util.Random(seed) on the device (seed from the clock when None)."""
+        if t < 0:
+            raise ValueError("temperature must be >= 0")
+        if seed is None:
+            import time
+            seed = time.time_ns() & 0x7FFFFFFFFFFFFFFF
+        self._o.native.set_sampling(float(t), 1.0, int(seed), 0)
+        self.temperature = float(t)
 
     def next(self) -> int:
         if self.currentStep < self.promptLength:
@@ -195,8 +203,7 @@ class AutoregressiveModel:
             if self._next_token is None:
                 raise RuntimeError("no previous output to sample from")
             tok = self._next_token
-        _, am = self._o.native.decode_step([tok], [self.currentStep], want_logits=False)
-        self._next_token = int(am[0])
+        self._next_token = int(self._o.native.decode_sample([tok], [self.currentStep])[0])
         self.currentToken = tok
         self.currentStep += 1
         self._o.position[0] = self.currentStep
@@ -245,11 +252,13 @@ class Qwen3:
     def getTokenEmbeddings(self):
         return None if self.stateDict is None else self.stateDict.get("model.embed_tokens.weight")
 
-    def setTemperature(self, t: float):
-        self.model.setTemperature(t)
+    def setTemperature(self, t: float, seed: int | None = None):
+        """Qwen3.setTemperature (Qwen3.java:285-291): 0 for greedy decoding."""
+        self.model.setTemperature(t, seed)
 
     def generate(self, prompt_tokens, steps: int) -> np.ndarray:
-        """Greedy generation of `steps` tokens (prompt included) entirely on the device."""
+        """Generation of `steps` tokens (prompt included) entirely on the device, greedy or sampled per
+        setTemperature."""
         return self.native.generate(np.asarray(prompt_tokens, np.int32), steps)
 
     def close(self):

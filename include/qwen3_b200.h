@@ -155,6 +155,21 @@ qw_status qw_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, i
 qw_status qw_generate(qw_model *m, const int32_t *prompts, int32_t batch, int32_t prompt_len,
                       int32_t steps, int32_t *tokens_out);
 
+/* Sampling for qw_generate and qw_decode_sample (AutoregressiveModel.setTemperature,
+ * engine/ml/src/main/java/org/almostrealism/ml/AutoregressiveModel.java:47-61).  temperature <= 0:
+ * greedy (the default).  mode 0: the sampler Qwen3 generates with (AutoregressiveModel.of, :405-434:
+ * softmax of logits / temperature, then sampleToken(probabilities, vocab, 1.0, 1.0, random), which
+ * applies a second softmax); mode 1: sampleToken(logits, vocab, temperature, top_p, random) (:323-386,
+ * nucleus filtering when top_p < 1).  Slot s draws from its own java.util.Random(seed + s) sequence
+ * (the same 48-bit generator, so a Java caller seeding identically draws the same numbers). */
+qw_status qw_set_sampling(qw_model *m, double temperature, double top_p, int64_t seed, int32_t mode);
+
+/* One decode step like qw_decode_step, with the next token drawn by the model's sampling settings
+ * (greedy when the temperature is 0) into tokens_out (batch).  Stands in for AutoregressiveModel.next
+ * after the prompt (AutoregressiveModel.java:295-308). */
+qw_status qw_decode_sample(qw_model *m, const int32_t *tokens, const int32_t *slots, const int32_t *positions,
+                           int32_t batch, int32_t *tokens_out);
+
 /* Device-resident variant of qw_decode_step for benchmarking and graph replay:
  * all pointers are device pointers; enqueued on the model's stream.  Pages must
  * already be reserved (qw_reserve).  If advance != 0 the kernel writes the argmax
@@ -231,6 +246,14 @@ qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_t vocab, in
 enum { QW_LINEAR_STORE = 0, QW_LINEAR_RESID = 1, QW_LINEAR_SWIGLU = 2 };
 qw_status qw_op_linear(const void *w, int32_t n_out, int32_t k, const void *x, int32_t t, int32_t epi,
                        const float *bias, const float *resid, void *out, void *stream);
+
+/* Token sampling over caller-provided device buffers: rows of logits (rows, ld) fp32, one uniform draw
+ * in [0, 1) per row (r_uniform, device), scratch (rows, vocab) doubles; tokens_out (rows) int32.
+ * temperature <= 0 is the first-index argmax; mode as for qw_set_sampling.  Stands in for
+ * AutoregressiveModel.sampleToken (AutoregressiveModel.java:323-386) and the sampler of
+ * AutoregressiveModel.of (:405-434), given the random draw. */
+qw_status qw_op_sample(const float *logits, int32_t rows, int32_t vocab, int32_t ld, double temperature, double top_p,
+                       int32_t mode, const double *r_uniform, double *scratch, int32_t *tokens_out, void *stream);
 
 /* qw_op_lm_head_argmax with no allocation anywhere: same arguments, results and errors,
  * but its cross-CTA scratch is a fixed 64 KiB array compiled into the library (held on every

@@ -224,3 +224,56 @@ class OracleModel:
         if r:
             raise ValueError("oracle: generate failed")
         return toks, last
+
+
+# ------------------------------------------------------------------ sampling (test infrastructure)
+class JavaRandom:
+    """java.util.Random restated (the published 48-bit linear congruential generator), so that tests can
+    reproduce the draws of a Java caller seeding new Random(seed)."""
+
+    MASK = (1 << 48) - 1
+
+    def __init__(self, seed: int):
+        self.s = (seed ^ 0x5DEECE66D) & self.MASK
+
+    def next(self, bits: int) -> int:
+        self.s = (self.s * 0x5DEECE66D + 0xB) & self.MASK
+        v = self.s >> (48 - bits)
+        return v - (1 << 32) if v >= (1 << 31) else v  # Java's (int) cast
+
+    def next_double(self) -> float:
+        return ((self.next(26) << 27) + self.next(27)) * 2.0 ** -53
+
+
+def sample_token(values, vocab: int, temperature: float, top_p: float, r: float | None) -> int:
+    """AutoregressiveModel.sampleToken (engine/ml/src/main/java/org/almostrealism/ml/AutoregressiveModel.java:323-386)
+    in double precision, with the uniform draw r given (None or temperature <= 0: greedy first max)."""
+    v = np.asarray(values, np.float64)[:vocab]
+    if temperature <= 0.0 or r is None:
+        return int(np.argmax(v))  # numpy's argmax keeps the first maximum, like the strict > loop
+    probs = v / temperature
+    probs = np.exp(probs - probs.max())
+    probs = probs / probs.sum()
+    if top_p < 1.0:
+        order = np.argsort(-probs, kind="stable")  # Arrays.sort with a comparator is stable
+        cum = np.cumsum(probs[order])
+        cutoff = int(np.searchsorted(cum >= top_p, True)) + 1 if (cum >= top_p).any() else vocab
+        top_sum = float(cum[cutoff - 1])
+        keep = np.zeros(vocab, bool)
+        keep[order[:cutoff]] = True
+        probs = np.where(keep, probs, 0.0) / top_sum
+    cumulative = np.cumsum(probs)
+    idx = int(np.searchsorted(cumulative, r, side="right"))  # first i with r < cumulative[i]
+    return min(idx, vocab - 1)
+
+
+def sample_qwen3(logits, vocab: int, temperature: float, r: float | None) -> int:
+    """The sampler Qwen3 generates with (AutoregressiveModel.of, AutoregressiveModel.java:405-434): logits divided by
+    the temperature, softmax, then sampleToken(probabilities, vocab, 1.0, 1.0, random) -- a second softmax."""
+    v = np.asarray(logits, np.float64)[:vocab]
+    if temperature <= 0.0 or r is None:
+        return int(np.argmax(v))
+    p = v / temperature
+    p = np.exp(p - p.max())
+    p = p / p.sum()
+    return sample_token(p, vocab, 1.0, 1.0, r)

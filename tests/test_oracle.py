@@ -254,3 +254,59 @@ def test_golden_fixture_regression():
     m.load_state_dict(sd)
     got = np.array([m.forward_token(t, p) for p, t in enumerate(g["tokens"])])
     np.testing.assert_allclose(got, g["logits"], rtol=1e-6, atol=1e-7)
+
+
+# ---------------------------------------------------------------- sampling restatements
+def test_java_random_known_answers():
+    """java.util.Random known answers: new Random(0).nextDouble(), new Random(42).nextDouble() (twice) and
+    new Random(42).nextInt()."""
+    r = O.JavaRandom(0)
+    assert r.next_double() == 0.730967787376657
+    r = O.JavaRandom(42)
+    assert r.next_double() == 0.7275636800328681
+    assert r.next_double() == 0.6832234717598454
+    assert O.JavaRandom(42).next(32) == -1170105035
+
+
+def test_sample_token_matches_direct_loops():
+    """sampleToken restated with numpy against a literal loop transcription of its steps."""
+    rng = np.random.default_rng(11)
+    for trial in range(20):
+        V = 50
+        logits = rng.normal(size=V) * 3
+        T, top_p, r = [0.7, 1.3][trial % 2], [0.3, 0.9, 1.0][trial % 3], rng.random()
+        probs = [x / T for x in logits]
+        m = max(probs)
+        probs = [math.exp(x - m) for x in probs]
+        s = sum(probs)
+        probs = [x / s for x in probs]
+        if top_p < 1.0:
+            idx = sorted(range(V), key=lambda i: -probs[i])
+            cum = 0.0
+            top_sum = 0.0
+            cutoff = V
+            for i in range(V):
+                cum += probs[idx[i]]
+                top_sum += probs[idx[i]]
+                if cum >= top_p:
+                    cutoff = i + 1
+                    break
+            for i in range(cutoff, V):
+                probs[idx[i]] = 0.0
+            probs = [x / top_sum for x in probs]
+        want, c = V - 1, 0.0
+        for i in range(V):
+            c += probs[i]
+            if r < c:
+                want = i
+                break
+        assert O.sample_token(logits, V, T, top_p, r) == want
+
+
+def test_sample_greedy_and_ties():
+    v = np.array([0.5, 2.0, 2.0, -1.0])
+    assert O.sample_token(v, 4, 0.0, 1.0, 0.3) == 1
+    assert O.sample_qwen3(v, 4, 0.0, 0.3) == 1
+    # equal probabilities keep index order inside the nucleus: the two tied maxima at top_p 0.4
+    v = np.array([1.0, 3.0, 3.0, 0.0])
+    assert O.sample_token(v, 4, 1.0, 0.4, 0.999) == 1
