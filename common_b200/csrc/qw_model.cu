@@ -25,7 +25,7 @@ using namespace qw;
 namespace {
 
 enum Kind {
-    K_EMBED = 0, K_LMHEAD = 1, K_NORM = 2,
+    K_EMBED = 0, K_LMHEAD = 1, K_NORM = 2, K_FREQ = 3,
     K_RMS_ATT = 0, K_RMS_FFN, K_WQ, K_WK, K_WV, K_WO, K_BQ, K_BK, K_BV, K_QN, K_KN, K_W1, K_W3, K_W2, K_NUM_LAYER_KINDS
 };
 const char *kLayerNames[K_NUM_LAYER_KINDS] = {
@@ -208,6 +208,14 @@ int resolve(qw_model *m, const char *key, Target &t) {
         t.full_rows = 1; t.full_cols = D; t.rows = 1; t.cols = D;
         t.dst = m->norm_final; t.dst_ld = D; t.tensor_id = 2; t.is_norm = true;
         t.loaded = &m->top_loaded; t.bit = 1u << K_NORM;
+        return 0;
+    }
+    if (!strcmp(key, "rope.freq_cis")) {
+        // an explicit RoPE table (seq_len, head_dim / 2, 2) = (cos, sin), as Llama2 checkpoints carry
+        // (Llama2Weights.java freqCis); replaces the one computed from rope_theta.  Optional.
+        t.full_rows = 1; t.full_cols = (long long)c.seq_len * c.head_dim; t.rows = 1; t.cols = c.seq_len * c.head_dim;
+        t.dst = m->freq; t.dst_ld = t.cols; t.tensor_id = 3;
+        t.loaded = &m->top_loaded; t.bit = 1u << K_FREQ;
         return 0;
     }
     int l = -1, n = 0;

@@ -123,12 +123,12 @@ def synthetic_state_dict(cfg: Qwen3Config, seed: int = 0, std: float = 0.02) -> 
 
 
 def native_config(cfg: Qwen3Config, precision: str = "bf16", kv_precision: str | None = None, max_batch: int = 1,
-                  max_tokens: int = 0, page_size: int = 64) -> native.QwConfig:
+                  max_tokens: int = 0, page_size: int = 64, eps: float = 1e-6) -> native.QwConfig:
     dt = {"bf16": native.DTYPE_BF16, "fp32": native.DTYPE_F32}
     kv = kv_precision or precision
     return native.make_config(cfg.dim, cfg.hiddenDim, cfg.layerCount, cfg.headCount, cfg.kvHeadCount, cfg.headSize,
                               cfg.vocabSize, cfg.seqLen, cfg.sharedWeights, cfg.qkNorm, cfg.hasQkvBias, dt[precision],
-                              dt[kv], max_batch, max_tokens, page_size, 0, cfg.ropeTheta, 1e-6)
+                              dt[kv], max_batch, max_tokens, page_size, 0, cfg.ropeTheta, eps)
 
 
 class CompiledModel:
@@ -203,7 +203,12 @@ class AutoregressiveModel:
             if self._next_token is None:
                 raise RuntimeError("no previous output to sample from")
             tok = self._next_token
-        self._next_token = int(self._o.native.decode_sample([tok], [self.currentStep])[0])
+        if self.currentStep < self.promptLength - 1:
+            # inside the prompt the output is not sampled (the reference draws only once the prompt is fed)
+            _, am = self._o.native.decode_step([tok], [self.currentStep], want_logits=False)
+            self._next_token = int(am[0])
+        else:
+            self._next_token = int(self._o.native.decode_sample([tok], [self.currentStep])[0])
         self.currentToken = tok
         self.currentStep += 1
         self._o.position[0] = self.currentStep
@@ -216,12 +221,12 @@ class Qwen3:
     def __init__(self, config: Qwen3Config, stateDict: StateDictionary | None, tokenizer=None, *,
                  precision: str = "bf16", kv_precision: str | None = None, device: int = 0, max_batch: int = 1,
                  max_tokens: int = 0, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
-                 synthetic_seed: int | None = None, synthetic_std: float = 0.02):
+                 synthetic_seed: int | None = None, synthetic_std: float = 0.02, eps: float = 1e-6):
         self.config = config
         self.stateDict = stateDict
         self.tokenizer = tokenizer
         self.position = np.zeros(1, np.int32)
-        ncfg = native_config(config, precision, kv_precision, max_batch, max_tokens)
+        ncfg = native_config(config, precision, kv_precision, max_batch, max_tokens, eps=eps)
         self.native = native.NativeModel(ncfg, device, tp_rank, tp_size, nccl_id)
         if stateDict is not None:
             for k, v in stateDict.items():

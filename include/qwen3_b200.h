@@ -101,7 +101,9 @@ qw_status qw_get_unique_id(void *out128);
 qw_status qw_create(const qw_config *cfg, int32_t device, int32_t tp_rank, int32_t tp_size,
                     const void *nccl_unique_id, qw_model **out);
 
-/* Copy one state-dict tensor (HF key, Qwen3.java:361-382) from host memory.  The
+/* Copy one state-dict tensor (HF key, Qwen3.java:361-382) from host memory.  Besides the HF keys,
+ * "rope.freq_cis" (seq_len, head_dim / 2, 2) replaces the RoPE table computed from rope_theta (Llama2
+ * checkpoints carry theirs, engine/ml/src/main/java/org/almostrealism/ml/llama2/Llama2Weights.java).  The
  * rank keeps only its shard.  Accepts F32, BF16 or F64 host data and converts to the
  * configured storage type.  Stands in for StateDictionary.get
  * (engine/ml/src/main/java/org/almostrealism/ml/StateDictionary.java:119-150). */

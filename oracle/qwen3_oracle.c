@@ -288,6 +288,8 @@ static real *lookup(oref_model *m, const char *key, size_t *n) {
     if (!strcmp(key, "model.embed_tokens.weight")) { *n = (size_t)c->vocab * D; return m->embed; }
     if (!strcmp(key, "lm_head.weight")) { *n = (size_t)c->vocab * D; return c->shared_weights ? NULL : m->wcls; }
     if (!strcmp(key, "model.norm.weight")) { *n = D; return m->rms_final; }
+    /* an explicit RoPE table (seq_len, head_dim/2, 2), as Llama2 checkpoints carry (Llama2Weights.java:108-110) */
+    if (!strcmp(key, "rope.freq_cis")) { *n = (size_t)c->seq_len * c->head_dim; return m->freq; }
     if (sscanf(key, "model.layers.%d.%127s", &l, rest) != 2 || l < 0 || l >= c->layers) return NULL;
     if (c->share_layers && l > 0) return NULL;
     oref_layer *L = &m->L[l];
