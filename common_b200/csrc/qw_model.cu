@@ -772,6 +772,14 @@ qw_status sample_launch(qw_model *m, const float *logits, int batch, int *out, i
 
 }  // namespace
 
+namespace qw {
+// records an error message for qw_last_error from host code outside this file
+void model_set_error(qw_model *m, const std::string &msg) {
+    if (m) m->err = msg;
+}
+}  // namespace qw
+
+
 // ==========================================================================================
 // C ABI
 // ==========================================================================================

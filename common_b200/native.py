@@ -21,7 +21,8 @@ DTYPE_F32, DTYPE_BF16, DTYPE_F64 = 0, 1, 2
 QKNORM_NONE, QKNORM_VECTOR, QKNORM_HEAD = 0, 1, 2
 
 # every symbol include/qwen3_b200.h declares
-EXPORTS = ("qw_abi_version", "qw_build_info", "qw_get_unique_id", "qw_create", "qw_load_tensor", "qw_init_synthetic",
+EXPORTS = ("qw_abi_version", "qw_build_info", "qw_get_unique_id", "qw_create", "qw_load_tensor", "qw_load_state_dict_pb",
+           "qw_init_synthetic",
            "qw_finalize_weights", "qw_reset", "qw_reserve", "qw_decode_step", "qw_forward_hidden", "qw_prefill",
            "qw_generate", "qw_decode_step_device", "qw_capture_decode", "qw_replay_decode", "qw_synchronize",
            "qw_stream", "qw_last_launch_count", "qw_last_error", "qw_destroy", "qw_profile_decode",
@@ -64,6 +65,7 @@ def load() -> C.CDLL:
         "qw_get_unique_id": (I32, [P]),
         "qw_create": (I32, [C.POINTER(QwConfig), I32, I32, I32, P, C.POINTER(P)]),
         "qw_load_tensor": (I32, [P, C.c_char_p, I32, C.POINTER(C.c_int64), I32, P]),
+        "qw_load_state_dict_pb": (I32, [P, C.c_char_p, C.POINTER(I32)]),
         "qw_init_synthetic": (I32, [P, C.c_uint64, C.c_float]),
         "qw_finalize_weights": (I32, [P]),
         "qw_reset": (I32, [P, I32]),
@@ -210,6 +212,12 @@ class NativeModel:
             dt = DTYPE_F32
         dims = (C.c_int64 * a.ndim)(*a.shape)
         self._check(self.L.qw_load_tensor(self.h, key.encode(), dt, dims, a.ndim, a.ctypes.data_as(C.c_void_p)))
+
+    def load_state_dict_pb(self, path: str) -> int:
+        """Load a CollectionLibraryData file or directory; returns the number of tensors loaded."""
+        n = C.c_int32(0)
+        self._check(self.L.qw_load_state_dict_pb(self.h, os.fsencode(path), C.byref(n)))
+        return n.value
 
     def init_synthetic(self, seed: int, std: float):
         self._check(self.L.qw_init_synthetic(self.h, seed, std))

@@ -10,11 +10,12 @@ Every call goes through the C ABI; there is no Python or CPU implementation of t
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import numpy as np
 
-from . import native
+from . import collections_pb, native
 
 BOS_TOKEN = 151643  # Qwen3Tokenizer.java:76
 EOS_TOKEN = 151645  # Qwen3Tokenizer.java:79
@@ -53,38 +54,62 @@ class Qwen3Config:
 
 
 class StateDictionary:
-    """Weights by HF key (numpy arrays; float32, float64 or raw-bf16 uint16)."""
+    """Weights by HF key: StateDictionary(weights) over numpy arrays (float32, float64 or raw-bf16 uint16),
+    or StateDictionary(weightsDirectory) over the reference's protobuf files (a directory, or one file),
+    whose tensors are decoded when asked for (StateDictionary.java:63-150).  A model built from a
+    directory-backed dictionary loads the files through the library (qw_load_state_dict_pb)."""
 
-    def __init__(self, weights: dict):
-        self._w = dict(weights)
+    def __init__(self, weights):
+        if isinstance(weights, (str, os.PathLike)):
+            self.weightsDirectory = os.fspath(weights)
+            self._lazy = collections_pb.read_directory(self.weightsDirectory)
+            self._w = {}
+        else:
+            self.weightsDirectory = None
+            self._lazy = {}
+            self._w = dict(weights)
 
     def get(self, key: str):
+        if key not in self._w and key in self._lazy:
+            self._w[key] = self._lazy[key].numpy()
         return self._w.get(key)
 
+    def shape(self, key: str):
+        """The tensor's shape without decoding it (None when absent)."""
+        if key in self._lazy:
+            return self._lazy[key].shape
+        v = self._w.get(key)
+        return None if v is None else tuple(v.shape)
+
     def containsKey(self, key: str) -> bool:
-        return key in self._w
+        return key in self._w or key in self._lazy
 
     def keySet(self):
-        return self._w.keys()
+        return (self._lazy.keys() | self._w.keys()) if self._lazy else self._w.keys()
 
     def items(self):
-        return self._w.items()
+        return ((k, self.get(k)) for k in self.keySet())
+
+    def save(self, path: str, precision: str = "fp32"):
+        """StateDictionary.save(weights, path, precision) (StateDictionary.java:215-235)."""
+        collections_pb.save({k: self.get(k) for k in self.keySet()}, path, precision)
 
 
 def infer_config(sd: StateDictionary, headSize: int | None = None) -> Qwen3Config:
     """Qwen3.inferConfig equivalent (Qwen3.java:200-240): geometry from tensor shapes."""
-    emb = sd.get("model.embed_tokens.weight")
-    vocab, dim = emb.shape
+    vocab, dim = sd.shape("model.embed_tokens.weight")
     layers = 0
     while sd.containsKey(f"model.layers.{layers}.input_layernorm.weight"):
         layers += 1
-    hidden = sd.get("model.layers.0.mlp.gate_proj.weight").shape[0]
-    q_rows = sd.get("model.layers.0.self_attn.q_proj.weight").shape[0]
-    kv_rows = sd.get("model.layers.0.self_attn.k_proj.weight").shape[0]
-    qn = sd.get("model.layers.0.self_attn.q_norm.weight")
+    hidden = sd.shape("model.layers.0.mlp.gate_proj.weight")[0]
+    q_rows = sd.shape("model.layers.0.self_attn.q_proj.weight")[0]
+    kv_rows = sd.shape("model.layers.0.self_attn.k_proj.weight")[0]
+    qn = sd.shape("model.layers.0.self_attn.q_norm.weight")
     if headSize is None:
-        headSize = qn.shape[-1] if qn is not None and qn.ndim == 2 else 128
-    shared = (not sd.containsKey("lm_head.weight")) or sd.get("lm_head.weight") is emb
+        headSize = qn[-1] if qn is not None and len(qn) == 2 else 128
+    # identity of the two arrays, as Qwen3.java:230-231 compares references (never true for decoded files)
+    shared = not sd.containsKey("lm_head.weight") or (
+        sd.weightsDirectory is None and sd.get("lm_head.weight") is sd.get("model.embed_tokens.weight"))
     return Qwen3Config(dim, hidden, layers, q_rows // headSize, kv_rows // headSize, vocab, 131072, shared, 1e6,
                        headSize=headSize, qkNorm=native.QKNORM_VECTOR if qn is not None else native.QKNORM_NONE,
                        hasQkvBias=sd.containsKey("model.layers.0.self_attn.q_proj.bias"))
@@ -228,7 +253,9 @@ class Qwen3:
         self.position = np.zeros(1, np.int32)
         ncfg = native_config(config, precision, kv_precision, max_batch, max_tokens, eps=eps)
         self.native = native.NativeModel(ncfg, device, tp_rank, tp_size, nccl_id)
-        if stateDict is not None:
+        if stateDict is not None and stateDict.weightsDirectory is not None:
+            self.native.load_state_dict_pb(stateDict.weightsDirectory)
+        elif stateDict is not None:
             for k, v in stateDict.items():
                 self.native.load_tensor(k, v)
         elif synthetic_seed is not None:

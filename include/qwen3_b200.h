@@ -110,6 +110,18 @@ qw_status qw_create(const qw_config *cfg, int32_t device, int32_t tp_rank, int32
 qw_status qw_load_tensor(qw_model *m, const char *key, qw_dtype dtype, const int64_t *dims,
                          int32_t ndims, const void *host_ptr);
 
+/* Load the reference's protobuf state dictionary: `path` is one CollectionLibraryData file or a
+ * directory whose non-hidden regular files each hold one (read in name order), as
+ * StateDictionary(weightsDirectory) does (engine/ml/src/main/java/org/almostrealism/ml/StateDictionary.java:119-150,
+ * message types in engine/ml/src/main/proto/collections.proto).  Each entry is decoded as
+ * CollectionEncoder.decode does (`data` doubles when present, else `data_32` floats; an entry without
+ * dimensions is skipped) and passed to qw_load_tensor; keys this model does not use are skipped.  As in
+ * StateDictionary.loadWeights, a file that cannot be parsed, or an entry whose value count does not match its
+ * dimensions, ends that file with a warning (stderr and qw_last_error; the call still returns QW_OK) and
+ * loading continues with the next file.  A known key whose shape does not fit the model returns its
+ * qw_load_tensor error.  *loaded_out (may be NULL) receives the number of tensors loaded. */
+qw_status qw_load_state_dict_pb(qw_model *m, const char *path, int32_t *loaded_out);
+
 /* Fill every weight on the device from the counter-based synthetic generator
  * (seed, std); all rmsnorm / q_norm / k_norm weights are set to 1. */
 qw_status qw_init_synthetic(qw_model *m, uint64_t seed, float std);
