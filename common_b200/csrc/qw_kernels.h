@@ -180,6 +180,7 @@ struct StepArgs {
     int stage_off;                   // floats: staged attention keys within the activation region
     int kv_bf16;
     unsigned long long *trace;       // optional: CTA 0's globaltimer before / after every grid barrier
+    int evict_first;                 // weight stream marked L2 evict-first (keeps code, KV and activations resident)
 };
 
 size_t step_smem_bytes(const StepArgs &a);

@@ -9,6 +9,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <algorithm>
 #include <string>
@@ -978,8 +979,12 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 sa.bar = m->d_bar;
                 sa.ss = reinterpret_cast<float *>(m->d_bar + 1);
                 sa.counters = m->d_bar + 1 + 2 * c.layers;
-                AL(m->d_trace, (size_t)2 * (5 * c.layers + 2));
+                AL(m->d_trace, (size_t)2 * (5 * c.layers + 2) + (size_t)8 * c.layers);
                 sa.err = m->pf.d_err;
+                {
+                    const char *ev = getenv("QW_STEP_EVICT");
+                    sa.evict_first = ev ? atoi(ev) : 1;
+                }
                 sa.tp = tp_size; sa.rank = tp_rank; sa.v0 = m->v0;
                 sa.q_total = c.heads * c.head_dim; sa.kv_total = c.kv_heads * c.head_dim;
                 sa.x2 = m->xb;
@@ -1312,6 +1317,28 @@ qw_status qw_profile_decode(qw_model *m, int32_t batch, float *ms_out, int32_t *
                 ms_out[n] = (float)((double)(tr[2 * i + 2] - tr[2 * i + 1]) * 1e-6);
                 kinds_out[n++] = QW_KERNEL_OTHER;
             }
+        }
+        if (getenv("QW_TRACE_ATTN")) {
+            // development aid: mean sub-phase times of CTA 0's attention item over the layers
+            std::vector<unsigned long long> at((size_t)8 * m->c.layers);
+            CK(cudaMemcpy(at.data(), m->d_trace + tr.size(), sizeof(unsigned long long) * at.size(),
+                          cudaMemcpyDeviceToHost));
+            double sum[7] = {0};
+            for (int l = 0; l < m->c.layers; l++) {
+                const unsigned long long start = tr[2 * (5 * l) + 2], end = tr[2 * (5 * l + 1) + 1];
+                unsigned long long prev = start;
+                for (int k = 0; k < 6; k++) {
+                    const unsigned long long t = at[(size_t)l * 8 + k];
+                    sum[k] += t >= prev ? (double)(t - prev) : 0.0;
+                    if (t >= prev) prev = t;
+                }
+                sum[6] += end >= prev ? (double)(end - prev) : 0.0;
+            }
+            fprintf(stderr, "attention sub-phases (us, mean of %d layers): qk-sums %.2f  q/k/v %.2f  rope+kv-write %.2f  "
+                    "keys %.2f  warp-merge+partials %.2f  split-wait %.2f  merge %.2f\n", m->c.layers,
+                    sum[0] / m->c.layers * 1e-3, sum[1] / m->c.layers * 1e-3, sum[2] / m->c.layers * 1e-3,
+                    sum[3] / m->c.layers * 1e-3, sum[4] / m->c.layers * 1e-3, sum[5] / m->c.layers * 1e-3,
+                    sum[6] / m->c.layers * 1e-3);
         }
         float ms = 0.f;
         CK(cudaEventElapsedTime(&ms, m->prof_ev[0], m->prof_ev[1]));

@@ -121,7 +121,7 @@ __host__ __device__ __forceinline__ int chunk_cols(int K) {
 
 // producer: this CTA's rows [r0, r1) of W (N, K), kRows rows at a time, each group in column chunks
 __device__ __forceinline__ bool produce(Ring &rg, const __nv_bfloat16 *W, int N, int K, volatile int *abort_flag,
-                                        int *err, uint32_t &issued, uint32_t &last_ph) {
+                                        int *err, uint32_t &issued, uint32_t &last_ph, uint64_t policy) {
     int r0, r1;
     split_rows(N, blockIdx.x, gridDim.x, r0, r1);
     const int C = chunk_cols(K);
@@ -134,9 +134,9 @@ __device__ __forceinline__ bool produce(Ring &rg, const __nv_bfloat16 *W, int N,
                          : "memory");
             for (int j = 0; j < nr; j++)
                 asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        su32(rg.buf + (size_t)rg.slot * kPiece + (size_t)j * C * 2)),
-                    "l"(W + (size_t)(ra + j) * K + c0), "r"((uint32_t)(C * 2)), "r"(fb)
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+                    "%4;" ::"r"(su32(rg.buf + (size_t)rg.slot * kPiece + (size_t)j * C * 2)),
+                    "l"(W + (size_t)(ra + j) * K + c0), "r"((uint32_t)(C * 2)), "r"(fb), "l"(policy)
                     : "memory");
             issued |= 1u << rg.slot;
             last_ph = (last_ph & ~(1u << rg.slot)) | (rg.ph << rg.slot);
@@ -531,6 +531,13 @@ __device__ __forceinline__ void stage_kv(const StepArgs &a, const StepLayer &Ly,
 // and key, the KV-cache write (split 0), online-softmax attention over its keys, partial or final
 // output, and the merge of all splits by the last CTA to finish this KV head.  The whole-vector
 // QK-norm uses the sums of squares the QKV phase accumulated (a.ss).
+// sub-phase timestamps of CTA 0's attention item (profiling runs only): slot k of layer `layer`,
+// after the per-phase pairs
+__device__ __forceinline__ void attn_mark(const StepArgs &a, int layer, int k) {
+    if (a.trace && blockIdx.x == 0 && threadIdx.x == 0)
+        a.trace[2 * (5 * a.layers + 1) + (size_t)layer * 8 + k] = trace_ns();
+}
+
 template <typename KT, int D, int G>
 __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int kvh, int sp, int ns, float *sm,
                           const KT *stage) {
@@ -567,6 +574,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         sck = 1.0f / sqrtf(tk / (float)a.kv_total + 1e-6f);
     }
     constexpr int NQ4 = G * D / 4, NK4 = D / 4;
+    attn_mark(a, layer, 0);
     asm volatile("cp.async.wait_all;" ::: "memory");  // this item's first key tile, staged during the QKV phase
     for (int i = tid; i < NQ4 + 2 * NK4; i += kStepConsumers) {
         float4 v;
@@ -591,6 +599,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         }
     }
     consumers_sync();
+    attn_mark(a, layer, 1);
     if (a.qk_mode == 2) {
         for (int hh = warp; hh <= G; hh += 8) {
             float *v = hh < G ? qs + hh * D : ks;
@@ -630,6 +639,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     if (sp == 0)
         for (int i = tid; i < D; i += kStepConsumers) Elt<KT>::store(vc + cbase + i, vs[i]);
     consumers_sync();
+    attn_mark(a, layer, 2);
     // ---- keys [t0, t1): warp w takes keys t0 + 64 j + 8 w .. + 7 ----
     float qreg[G][DPL];
 #pragma unroll
@@ -726,6 +736,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
             }
         }
     }
+    attn_mark(a, layer, 3);
     // ---- merge the 8 warps: warps 4..7 into warps 0..3, then the 4 through shared memory ----
     if (warp >= 4) {
 #pragma unroll
@@ -786,6 +797,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     // ---- every split CTA of this KV head waits for all partials, then merges its slice of the output ----
     __threadfence();
     consumers_sync();
+    attn_mark(a, layer, 4);
     unsigned *cnt = a.counters + (size_t)layer * a.Hkv + kvh;  // zeroed before the launch
     if (tid == 0) {
         atomicAdd(cnt, 1u);
@@ -796,6 +808,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         __threadfence();
     }
     consumers_sync();
+    attn_mark(a, layer, 5);
     const int per = (G * D + ns - 1) / ns;
     const int i0 = sp * per, i1 = min(G * D, i0 + per);
     // the (max, sum) of every split of the heads this slice touches, and the slice's partial outputs,
@@ -885,14 +898,21 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
         if (lane == 0) {
             uint32_t issued = 0, last_ph = 0;
             bool ok = true;
+            // the weights are read once per step: evict them first, so that L2 keeps the kernel's code, the
+            // KV cache and the activations (evict_normal when turned off)
+            uint64_t policy;
+            if (a.evict_first)
+                asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+            else
+                asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(policy));
             for (int l = 0; l < a.layers && ok; l++) {
                 const StepLayer &Ly = a.L[l];
-                ok = ok && produce(rg, Ly.w_qkv, QKV, D_, abort_flag, a.err, issued, last_ph);
-                ok = ok && produce(rg, Ly.w_o, D_, Q, abort_flag, a.err, issued, last_ph);
-                ok = ok && produce(rg, Ly.w_gu, 2 * F, D_, abort_flag, a.err, issued, last_ph);
-                ok = ok && produce(rg, Ly.w_down, D_, F, abort_flag, a.err, issued, last_ph);
+                ok = ok && produce(rg, Ly.w_qkv, QKV, D_, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce(rg, Ly.w_o, D_, Q, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce(rg, Ly.w_gu, 2 * F, D_, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce(rg, Ly.w_down, D_, F, abort_flag, a.err, issued, last_ph, policy);
             }
-            ok = ok && produce(rg, a.lm, a.V, D_, abort_flag, a.err, issued, last_ph);
+            ok = ok && produce(rg, a.lm, a.V, D_, abort_flag, a.err, issued, last_ph, policy);
             if (!ok) {
                 for (int i = 0; i < kRing; i++)
                     if (issued >> i & 1u) {
