@@ -531,6 +531,14 @@ __device__ __forceinline__ void stage_kv(const StepArgs &a, const StepLayer &Ly,
 // and key, the KV-cache write (split 0), online-softmax attention over its keys, partial or final
 // output, and the merge of all splits by the last CTA to finish this KV head.  The whole-vector
 // QK-norm uses the sums of squares the QKV phase accumulated (a.ss).
+// 2^x by the hardware approximation (ex2.approx, flushes subnormals): attention scores are kept in the
+// log2 domain (the scale carries log2 e), the usual flash-attention formulation
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // sub-phase timestamps of CTA 0's attention item (profiling runs only): slot k of layer `layer`,
 // after the per-phase pairs
 __device__ __forceinline__ void attn_mark(const StepArgs &a, int layer, int k) {
@@ -645,7 +653,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
-        for (int j = 0; j < DPL; j++) qreg[g][j] = qs[g * D + lane * DPL + j] * a.scale;
+        for (int j = 0; j < DPL; j++) qreg[g][j] = qs[g * D + lane * DPL + j] * (a.scale * 1.4426950408889634f);
     float m[G], l[G], o[G][DPL];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -709,13 +717,13 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
 #pragma unroll
             for (int j = 0; j < kStepTPW; j++) mx = fmaxf(mx, sc[j][g]);
             if (mx == -INFINITY) continue;
-            const float al = expf(m[g] - mx);
+            const float al = exp2_approx(m[g] - mx);
             l[g] *= al;
 #pragma unroll
             for (int e = 0; e < DPL; e++) o[g][e] *= al;
             m[g] = mx;
 #pragma unroll
-            for (int j = 0; j < kStepTPW; j++) sc[j][g] = expf(sc[j][g] - mx);
+            for (int j = 0; j < kStepTPW; j++) sc[j][g] = exp2_approx(sc[j][g] - mx);
         }
 #pragma unroll
         for (int j = 0; j < kStepTPW; j++) {
@@ -752,8 +760,8 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         for (int g = 0; g < G; g++) {
             const float om = wm[warp * G + g], ol = wl[warp * G + g];
             const float M = fmaxf(m[g], om);
-            const float ea = m[g] == -INFINITY ? 0.f : expf(m[g] - M);
-            const float eb = om == -INFINITY ? 0.f : expf(om - M);
+            const float ea = m[g] == -INFINITY ? 0.f : exp2_approx(m[g] - M);
+            const float eb = om == -INFINITY ? 0.f : exp2_approx(om - M);
             l[g] = l[g] * ea + ol * eb;
 #pragma unroll
             for (int j = 0; j < DPL; j++) o[g][j] = o[g][j] * ea + wo[(warp * G + g) * D + lane * DPL + j] * eb;
@@ -779,7 +787,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         if (M != -INFINITY) {
 #pragma unroll
             for (int w = 0; w < 4; w++) {
-                const float e = expf(wm[w * G + g] - M);
+                const float e = exp2_approx(wm[w * G + g] - M);
                 L += wl[w * G + g] * e;
                 O += wo[(w * G + g) * D + j] * e;
             }
@@ -841,7 +849,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
                 float L = 0.f;
                 for (int sidx = 0; sidx < ns; sidx++) {
                     const float pm = mlm[g * 64 + sidx];
-                    const float e = pm == -INFINITY ? 0.f : expf(pm - M);
+                    const float e = pm == -INFINITY ? 0.f : exp2_approx(pm - M);
                     L += mll[g * 64 + sidx] * e;
                     mlm[g * 64 + sidx] = e;
                 }

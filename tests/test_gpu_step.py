@@ -51,7 +51,11 @@ def test_step_kernel_equals_per_op_path():
         assert a.last_launch_count == 1
         lb, ib = b.decode_step([int(t)], [p])
         assert b.last_launch_count > 1
-        assert rel_l2(la[0], lb[0]) < 1e-4, p  # same math, different summation order
+        # same math with different summation orders and exp implementations (the step kernel's attention
+        # works in the log2 domain with ex2.approx); the few bf16 roundings of cached K / V rows that such
+        # differences flip accumulate over positions, so the bound is a few 1e-4 (parity with the reference
+        # is the oracle tests' 2e-2)
+        assert rel_l2(la[0], lb[0]) < 3e-4, p
     a.close()
     b.close()
 
