@@ -12,7 +12,7 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libqwen3_b200.so")
+LIB_PATH = os.environ.get("QW_LIB") or os.path.join(HERE, "lib", "libqwen3_b200.so")  # QW_LIB: another build
 
 QW_OK = 0
 STATUS_NAMES = {0: "QW_OK", 1: "QW_ERR_ARG", 2: "QW_ERR_SHAPE", 3: "QW_ERR_OOM", 4: "QW_ERR_CUDA", 5: "QW_ERR_NCCL",
