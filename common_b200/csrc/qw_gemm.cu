@@ -20,6 +20,10 @@
 // Tiles are visited in groups of 8 token tiles so that the CTAs running at the same time share
 // their W and X tiles in L2.
 //
+// Launched with programmatic dependent launch: the prologue (barriers, TMEM, descriptor prefetch)
+// and the first S weight tiles overlap the end of the previous kernel in the stream; the
+// activation tiles and the epilogue wait for it (griddepcontrol.wait).
+//
 // Every mbarrier wait is bounded (kTcWaitNs); on expiry the CTA records TC_DEVERR_TIMEOUT,
 // lets its issued copies and MMAs land, frees its TMEM and returns.
 #include <cuda.h>
@@ -202,6 +206,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
+    griddep_launch_dependents();  // the next kernel's prologue (and weight loads) may start
 
     const int nf = (a.M + kBM - 1) / kBM, nt = (a.T + BN - 1) / BN, nks = a.ksplit;
     const int nkb = (a.K + kBK - 1) / kBK;
@@ -213,18 +218,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int s = 0;
             uint32_t ph = 0, issued = 0, last_ph = 0;
             bool ok = true;
+            // The weights do not depend on the previous kernel in the stream: the first S stages load
+            // their W tiles before the programmatic-launch wait, their X tiles (the previous kernel's
+            // output) after it, into the same stage barrier.
+            bool waited = false;
+            int npend = 0, pend_kb[S], pend_t0[S];
+            auto flush = [&]() {
+                griddep_wait();
+                waited = true;
+                for (int i = 0; i < npend; i++)
+                    tma_load_2d(sB + i * B_BYTES, &tmX, &full_bar[i], pend_kb[i] * kBK, pend_t0[i] * BN);
+            };
             for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
                 const TileCoord c = tile_coord(tile, nf, nt, nks, nkb);
                 for (int kb = c.kb0; kb < c.kb1; kb++) {
                     if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, a.err)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full_bar[s], A_BYTES + B_BYTES);
                     tma_load_2d(sA + s * A_BYTES, &tmW, &full_bar[s], kb * kBK, c.f0);
-                    tma_load_2d(sB + s * B_BYTES, &tmX, &full_bar[s], kb * kBK, c.t0 * BN);
+                    if (waited) {
+                        tma_load_2d(sB + s * B_BYTES, &tmX, &full_bar[s], kb * kBK, c.t0 * BN);
+                    } else {  // stages 0..S-1 of the first pass, in order
+                        pend_kb[npend] = kb;
+                        pend_t0[npend] = c.t0;
+                        if (++npend == S) flush();
+                    }
                     issued |= 1u << s;
                     last_ph = (last_ph & ~(1u << s)) | (ph << s);
                     if (++s == S) { s = 0; ph ^= 1u; }
                 }
             }
+            if (!waited) flush();
             if (!ok) {
                 // let every issued copy land before the CTA's shared memory goes away
                 for (int i = 0; i < S; i++)
@@ -271,6 +294,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        griddep_wait();  // resid and out may belong to the previous kernel in the stream
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         int it = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
@@ -394,8 +418,7 @@ cudaError_t launch_bn(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs
     const int nf = (a.M + kBM - 1) / kBM, nt = (a.T + BN - 1) / BN;
     const int total = nf * nt * a.ksplit;
     const int grid = total < num_sms ? total : num_sms;
-    kfn<<<grid, kTcThreads, tc_smem_bytes(BN), st>>>(mw, mx, a);
-    return cudaGetLastError();
+    return launch_pdl(kfn, dim3(grid), dim3(kTcThreads), tc_smem_bytes(BN), st, mw, mx, a);
 }
 
 template <int EPI>

@@ -37,6 +37,7 @@ cudaError_t argmax_merge_launch(const float *vals, const int *idxs, int tp, int 
 cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, float *out, cudaStream_t st);
 cudaError_t hold_launch(unsigned long long ns, cudaStream_t st);
 cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cudaStream_t st);
+cudaError_t zero_launch(float *out, size_t n, cudaStream_t st);  // programmatically launched; memset when unaligned
 
 struct NormRowsArgs {
     float *x;  // (rows, ld_x) fp32 residual stream: read, or written when embed / part is given

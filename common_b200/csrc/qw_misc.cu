@@ -132,6 +132,22 @@ cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cud
     return cudaGetLastError();
 }
 
+// out[0, n) = 0 inside a chain of programmatically launched kernels (a memset node would end the
+// chain): the accumulator of a split-K GEMM that follows.
+__global__ void zero_kernel(float4 *out, size_t n4) {
+    griddep_launch_dependents();
+    griddep_wait();  // the previous kernel may still read the buffer
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+cudaError_t zero_launch(float *out, size_t n, cudaStream_t st) {
+    if (n % 4 || (reinterpret_cast<uintptr_t>(out) & 15)) return cudaMemsetAsync(out, 0, n * sizeof(float), st);
+    int grid = (int)((n / 4 + 255) / 256);
+    if (grid > 148 * 4) grid = 148 * 4;
+    if (grid < 1) grid = 1;
+    return launch_pdl(zero_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<float4 *>(out), n / 4);
+}
+
 // Bounded busy-wait of `ns` nanoseconds on the device (globaltimer), used to let the host
 // run ahead of the GPU before a profiled sequence of launches.  Ends by itself.
 __global__ void hold_kernel(unsigned long long ns) {

@@ -500,7 +500,7 @@ qw_status tc_gemm(qw_model *m, int kind, const void *W, const void *X, int M, in
     a.M = M; a.T = T; a.K = K;
     a.ksplit = allow_split ? tc_pick_ksplit(M, T, K, bn, m->num_sms) : 1;
     a.out = out; a.ld_out = ld_out; a.resid = resid; a.ld_resid = ld_out; a.bias = bias; a.err = m->pf.d_err;
-    if (a.ksplit > 1 && epi == TC_STORE) CK(cudaMemsetAsync(out, 0, sizeof(float) * (size_t)T * ld_out, m->st));
+    if (a.ksplit > 1 && epi == TC_STORE) CK(zero_launch((float *)out, (size_t)T * ld_out, m->st));
     LKK(kind, tc_gemm_launch(W, X, a, epi, bn, m->num_sms, m->st));
     return QW_OK;
 }

@@ -25,6 +25,8 @@ constexpr int kNormThreads = 256;
 constexpr size_t kPrepSmem = 160 * 1024;  // dynamic shared memory the row kernels are opted in to
 
 __global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(NormRowsArgs a) {
+    griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
+    griddep_wait();               // the previous kernel's results
     extern __shared__ __align__(16) float xrow[];
     __shared__ float red[kNormThreads / 32];
     const int r = blockIdx.x, K = a.K, tid = threadIdx.x;
@@ -67,8 +69,7 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
     if (rows < 1 || a.K % 4) return cudaErrorInvalidValue;
     size_t smem = sizeof(float) * a.K;
     if (smem > kPrepSmem) return cudaErrorInvalidValue;
-    norm_rows_kernel<<<rows, kNormThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(norm_rows_kernel, dim3(rows), dim3(kNormThreads), smem, st, a);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -78,6 +79,8 @@ constexpr int kPostThreads = 256;
 
 template <typename KT>
 __global__ void __launch_bounds__(kPostThreads) qkv_post_kernel(QkvPostArgs a) {
+    griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
+    griddep_wait();               // the previous kernel's results
     extern __shared__ __align__(16) float row[];  // q (Ql) | k (KVl) | v (KVl)
     __shared__ float red[2][kPostThreads / 32];
     __shared__ float s_sc[2];
@@ -150,9 +153,8 @@ cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaSt
     auto k16 = qkv_post_kernel<__nv_bfloat16>;
     auto k32 = qkv_post_kernel<float>;
     if (smem > kPrepSmem) return cudaErrorInvalidValue;
-    if (kv_bf16) k16<<<rows, kPostThreads, smem, st>>>(a);
-    else k32<<<rows, kPostThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return kv_bf16 ? launch_pdl(k16, dim3(rows), dim3(kPostThreads), smem, st, a)
+                   : launch_pdl(k32, dim3(rows), dim3(kPostThreads), smem, st, a);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -199,6 +201,8 @@ __device__ __forceinline__ uint32_t fa_off(int row, int chunk) {
 
 template <int D>
 __global__ void __launch_bounds__(kFaWarps * 32) flash_prefill_kernel(FlashArgs a) {
+    griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
+    griddep_wait();               // the previous kernel's results
     constexpr int CH = D / 8;  // 16-byte chunks per row
     extern __shared__ __align__(128) uint8_t fsm[];
     uint8_t *sK = fsm;                      // [2][64][D]
@@ -357,13 +361,10 @@ cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st) 
     dim3 grid((a.L + kFaRows - 1) / kFaRows, a.H, nseq);
     if (a.d == 128) {
         const size_t smem = 4 * kFaKeys * 128 * 2;
-        flash_prefill_kernel<128><<<grid, kFaWarps * 32, smem, st>>>(a);
-    } else if (a.d == 64) {
-        flash_prefill_kernel<64><<<grid, kFaWarps * 32, 4 * kFaKeys * 64 * 2, st>>>(a);
-    } else {
-        return cudaErrorInvalidValue;
+        return launch_pdl(flash_prefill_kernel<128>, grid, dim3(kFaWarps * 32), smem, st, a);
     }
-    return cudaGetLastError();
+    if (a.d == 64) return launch_pdl(flash_prefill_kernel<64>, grid, dim3(kFaWarps * 32), 4 * kFaKeys * 64 * 2, st, a);
+    return cudaErrorInvalidValue;
 }
 
 
@@ -377,6 +378,8 @@ constexpr int kFdStages = 3;
 
 template <int D, int G>
 __global__ void __launch_bounds__(kFaWarps * 32) flash_decode_kernel(FlashDecodeArgs a) {
+    griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
+    griddep_wait();               // the previous kernel's results
     constexpr int CH = D / 8;
     constexpr int TILE_BYTES = kFaKeys * D * 2;
     extern __shared__ __align__(128) uint8_t fsm[];
@@ -582,14 +585,14 @@ __global__ void __launch_bounds__(kFaWarps * 32) flash_decode_kernel(FlashDecode
 template <int D>
 static cudaError_t flash_decode_g(const FlashDecodeArgs &a, dim3 grid, cudaStream_t st) {
     const size_t smem = (size_t)kFdStages * 2 * kFaKeys * D * 2;
+    const dim3 block(kFaWarps * 32);
     switch (a.H / a.Hkv) {
-        case 1: flash_decode_kernel<D, 1><<<grid, kFaWarps * 32, smem, st>>>(a); break;
-        case 2: flash_decode_kernel<D, 2><<<grid, kFaWarps * 32, smem, st>>>(a); break;
-        case 4: flash_decode_kernel<D, 4><<<grid, kFaWarps * 32, smem, st>>>(a); break;
-        case 8: flash_decode_kernel<D, 8><<<grid, kFaWarps * 32, smem, st>>>(a); break;
+        case 1: return launch_pdl(flash_decode_kernel<D, 1>, grid, block, smem, st, a);
+        case 2: return launch_pdl(flash_decode_kernel<D, 2>, grid, block, smem, st, a);
+        case 4: return launch_pdl(flash_decode_kernel<D, 4>, grid, block, smem, st, a);
+        case 8: return launch_pdl(flash_decode_kernel<D, 8>, grid, block, smem, st, a);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st) {
@@ -604,6 +607,8 @@ cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st
 // rows_argmax: one CTA per logits row; first index of the maximum
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) rows_argmax_kernel(RowsArgmaxArgs a) {
+    griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
+    griddep_wait();               // the previous kernel's results
     __shared__ float sv[16];
     __shared__ int si[16];
     const int b = blockIdx.x, tid = threadIdx.x;
@@ -653,8 +658,7 @@ cudaError_t prefill_kernels_prepare() {
 }
 
 cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t st) {
-    rows_argmax_kernel<<<rows, 512, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(rows_argmax_kernel, dim3(rows), dim3(512), 0, st, a);
 }
 
 }  // namespace qw
