@@ -450,13 +450,22 @@ cudaError_t tc_prepare() {
 
 int tc_pick_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
 
+// K ranges per output tile for a skinny (decode) problem.  A CTA's time is about (work units it runs) x (k-blocks
+// per unit + the unit's epilogue, ~2 k-blocks of time for its atomic accumulation), so the split minimising
+// ceil(tiles x ks / SMs) x (ceil(k-blocks / ks) + 2) is taken: e.g. 32 tiles x 64 k-blocks -> 4 (one unit per
+// CTA), not 5 (160 units: a second unit on 12 CTAs doubles the time).
 int tc_pick_ksplit(int M, int T, int K, int bn, int num_sms) {
     const int tiles = ((M + kBM - 1) / kBM) * ((T + bn - 1) / bn);
     const int nkb = (K + kBK - 1) / kBK;
-    if (tiles >= num_sms / 2) return 1;
-    int ks = (num_sms + tiles - 1) / tiles;
-    ks = ks > nkb / 2 ? nkb / 2 : ks;  // at least two k-blocks per split
-    return ks < 1 ? 1 : ks;
+    if (tiles >= 2 * num_sms || (bn > 64 && tiles >= num_sms / 2)) return 1;  // prefill shapes: no split
+    int best_ks = 1;
+    long long best = -1;
+    for (int ks = 1; ks <= (nkb / 2 > 1 ? nkb / 2 : 1); ks++) {  // at least two k-blocks per split
+        const long long waves = ((long long)tiles * ks + num_sms - 1) / num_sms;
+        const long long cost = waves * ((nkb + ks - 1) / ks + 2);
+        if (best < 0 || cost < best) { best = cost; best_ks = ks; }
+    }
+    return best_ks;
 }
 
 cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int epi, int bn, int num_sms,

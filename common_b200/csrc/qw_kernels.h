@@ -38,6 +38,7 @@ cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, flo
 cudaError_t hold_launch(unsigned long long ns, cudaStream_t st);
 cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cudaStream_t st);
 cudaError_t zero_launch(float *out, size_t n, cudaStream_t st);  // programmatically launched; memset when unaligned
+cudaError_t swiglu_rows_launch(const float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st);
 
 struct NormRowsArgs {
     float *x;  // (rows, ld_x) fp32 residual stream: read, or written when embed / part is given

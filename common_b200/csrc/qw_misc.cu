@@ -148,6 +148,25 @@ cudaError_t zero_launch(float *out, size_t n, cudaStream_t st) {
     return launch_pdl(zero_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<float4 *>(out), n / 4);
 }
 
+// h[t][p] = up * silu(gate) for rows of the (2F) gate/up projection interleaved in blocks of 16 gate then 16 up
+// rows, as the GEMM's SwiGLU epilogue computes it (same expression), h bf16 (T, F).
+__global__ void swiglu_rows_kernel(const float *gu, int F, __nv_bfloat16 *h) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int t = blockIdx.y;
+    const float *row = gu + (size_t)t * 2 * F;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < F; p += gridDim.x * blockDim.x) {
+        const int b = p / kGuBlock, j = p % kGuBlock;
+        const float g = row[b * 2 * kGuBlock + j], u = row[b * 2 * kGuBlock + kGuBlock + j];
+        h[(size_t)t * F + p] = __float2bfloat16(u * __fdividef(g, 1.0f + __expf(-g)));
+    }
+}
+cudaError_t swiglu_rows_launch(const float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st) {
+    if (T < 1 || F < 1) return cudaErrorInvalidValue;
+    const int bx = (F + 255) / 256 < 8 ? (F + 255) / 256 : 8;
+    return launch_pdl(swiglu_rows_kernel, dim3(bx, T), dim3(256), 0, st, gu, F, h);
+}
+
 // Bounded busy-wait of `ns` nanoseconds on the device (globaltimer), used to let the host
 // run ahead of the GPU before a profiled sequence of launches.  Ends by itself.
 __global__ void hold_kernel(unsigned long long ns) {

@@ -88,6 +88,7 @@ struct qw_model {
     unsigned *d_bar = nullptr;
     size_t step_zero_words = 0;
     float *gu = nullptr;
+    float *gu_split = nullptr;  // (max_batch, 2 Fl) fp32: gate/up of a split-K batched decode projection
     unsigned long long *d_trace = nullptr;  // per-phase timestamps of a profiled step
     unsigned *xch = nullptr;                // this rank's exchange buffer (tensor parallel step kernel)
     std::vector<void *> xch_peer;           // peers' exchange buffers opened through CUDA IPC
@@ -584,7 +585,16 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         LK(norm_rows_launch(na, T, m->st));
         pending = nullptr;
         // ---- gate/up + SwiGLU, down (+ residual) ----
-        TRY(tc_gemm(m, QW_KERNEL_GATE_UP, Ly.w_gu, pf.act, 2 * m->Fl, T, D, TC_SWIGLU, pf.h, m->Fl, nullptr, nullptr, false));
+        if (!prefill && T <= m->B && m->gu_split && tc_pick_ksplit(2 * m->Fl, T, D, tc_pick_bn(T), m->num_sms) > 1) {
+            // too few output tiles to fill the GPU: split K into an fp32 buffer, then SwiGLU row by row (the
+            // SwiGLU epilogue needs whole sums)
+            TRY(tc_gemm(m, QW_KERNEL_GATE_UP, Ly.w_gu, pf.act, 2 * m->Fl, T, D, TC_STORE, m->gu_split, 2 * m->Fl, nullptr,
+                        nullptr, true));
+            LKK(QW_KERNEL_GATE_UP, swiglu_rows_launch(m->gu_split, T, m->Fl, pf.h, m->st));
+        } else {
+            TRY(tc_gemm(m, QW_KERNEL_GATE_UP, Ly.w_gu, pf.act, 2 * m->Fl, T, D, TC_SWIGLU, pf.h, m->Fl, nullptr, nullptr,
+                        false));
+        }
         if (tpm) {
             TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, m->part, D, nullptr, nullptr, true));
             TRY(allreduce(m, m->part, (size_t)T * D));
@@ -947,6 +957,7 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
     if (m->pf.tc) {
         CK(tc_prepare());
         CK(prefill_kernels_prepare());
+        AL(m->gu_split, (size_t)B * 2 * m->Fl);
     }
     // the persistent step kernel: automatic at tp 1; under tensor parallelism only when asked for
     // (decode_kernels 2), its cross-GPU barriers cost more than the NCCL path saves at these sizes
@@ -1453,7 +1464,7 @@ void qw_destroy(qw_model *m) {
     cudaFree(m->part_o); cudaFree(m->part_ml); cudaFree(m->qk_ss); cudaFree(m->counters); cudaFree(m->am_counter);
     cudaFree(m->am_pval); cudaFree(m->am_pidx); cudaFree(m->am_val); cudaFree(m->am_idx); cudaFree(m->am_val_all);
     cudaFree(m->am_idx_all); cudaFree(m->logits); cudaFree(m->logits_all); cudaFree(m->d_tokens); cudaFree(m->d_argmax);
-    cudaFree(m->d_step_layers); cudaFree(m->d_bar); cudaFree(m->gu); cudaFree(m->d_trace);
+    cudaFree(m->d_step_layers); cudaFree(m->d_bar); cudaFree(m->gu); cudaFree(m->gu_split); cudaFree(m->d_trace);
     for (void *q : m->xch_peer)
         if (q) cudaIpcCloseMemHandle(q);
     cudaFree(m->xch); cudaFree(m->d_xch); cudaFree(m->d_persist);
