@@ -283,8 +283,9 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned &target, volat
     target += gridDim.x;
     if (threadIdx.x == 0 && trace && blockIdx.x == 0) trace[2 * idx + 1] = trace_ns();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
+        // release: this CTA's writes (ordered before by the named barrier above) are visible to whoever acquires
+        // the count; the acquire polls order every later read after the other CTAs' writes
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const uint64_t t0 = now_ns();
         while (ld_acquire(bar) < target) {
             if (*abort_flag || ld_acquire(reinterpret_cast<unsigned *>(err)) != 0u) { *abort_flag = 1; break; }
@@ -294,7 +295,6 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned &target, volat
                 break;
             }
         }
-        __threadfence();
         if (trace && blockIdx.x == 0) trace[2 * idx + 2] = trace_ns();
     }
     consumers_sync();
