@@ -803,17 +803,16 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     }
     if (ns == 1) return;
     // ---- every split CTA of this KV head waits for all partials, then merges its slice of the output ----
-    __threadfence();
     consumers_sync();
     attn_mark(a, layer, 4);
     unsigned *cnt = a.counters + (size_t)layer * a.Hkv + kvh;  // zeroed before the launch
     if (tid == 0) {
-        atomicAdd(cnt, 1u);
+        // release-add: the partials written above (ordered by the named barrier) are visible to the acquirers
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
         const uint64_t w0 = now_ns();
         while (ld_acquire(cnt) < (unsigned)ns) {
             if (now_ns() - w0 > kStepWaitNs) { atomicExch(a.err, 3); break; }
         }
-        __threadfence();
     }
     consumers_sync();
     attn_mark(a, layer, 5);
