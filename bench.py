@@ -82,41 +82,53 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def peaks_of():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return {}
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
 # ----------------------------------------------------------------------------------- CPU arm
-def cpu_sample(steps: int, warmup: int, threads: int | None = None):
+def cpu_sample(tokens: int, warmup_slices: int, threads: int | None = None):
     """The oracle port on the host cores: the 8B geometry in fp32 with one layer's weights shared by all
-    36 layers (identical bytes streamed per layer, 34 GB less host memory), context 512.  One sample =
-    one layer + 1/36 of the lm_head rows, so 36 samples = one decode token."""
+    36 layers (identical bytes streamed per layer, 34 GB less host memory), context 512.  One decode
+    token = 36 layer slices, each followed by 1/36 of the lm_head rows; `tokens` whole tokens are timed.
+    threads: OpenMP threads (default: every host core, whatever OMP_NUM_THREADS says)."""
     from oracle import oracle as O
-    if threads:
-        os.environ["OMP_NUM_THREADS"] = str(threads)
+    O.set_threads(threads or os.cpu_count() or 1)
     c = dict(GEOM_8B, seq_len=PROMPT + 64, share_layers=1)
     m = O.OracleModel(c, "f32")
     m.init_synthetic(0, 0.02)
     L, V = c["layers"], c["vocab"]
     rows = [(V * i) // L for i in range(L + 1)]
-    for i in range(warmup):
+    for i in range(warmup_slices):
         m.bench_slice(i % L, PROMPT, rows[i % L], rows[i % L + 1])
-    t0 = time.perf_counter()
-    for i in range(steps):
-        m.bench_slice(i % L, PROMPT, rows[i % L], rows[i % L + 1])
-    dt = time.perf_counter() - t0
+    per_token = []
+    for _ in range(tokens):
+        t0 = time.perf_counter()
+        for i in range(L):
+            m.bench_slice(i, PROMPT, rows[i], rows[i + 1])
+        per_token.append(time.perf_counter() - t0)
     m.close()
-    tok_s = steps / L / dt
-    return tok_s, dt, O.num_threads()
+    dt = sum(per_token)
+    return tokens / dt, dt, O.num_threads("f32")
 
 
 def run_reference(args):
+    """The reference arm: the Java reference cannot run on this image (no JDK), so its CPU path is the
+    oracle port, on every host core, one whole decode token per step."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    tok_s, dt, cores = cpu_sample(args.steps, args.warmup)
-    sample = (f"oracle port (fp32, OpenMP) at the Qwen3-8B geometry, layer weights shared, context {PROMPT}; "
-              f"{args.steps} samples of one layer + 1/36 lm_head = {args.steps / 36:.2f} tokens")
+    tok_s, dt, cores = cpu_sample(args.steps, 36 * args.warmup)
+    sample = (f"oracle port (fp32, OpenMP, {cores} threads) at the Qwen3-8B geometry, layer weights shared, "
+              f"context {PROMPT}; {args.steps} whole decode tokens (36 layers + full lm_head each), "
+              f"{dt:.1f} s")
     line = {"metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -237,6 +249,134 @@ def run_batched(args, rank, world, local, nid, peaks):
     m.close()
     return {"prefill": prefill, "decode_b%d" % B: decode}
 
+# ----------------------------------------------------------------------------------- parity gate
+# the model of tests/golden/make_tp_parity.py (2 layers, hidden 1024, 32 Q / 8 KV heads of 128, intermediate
+# 4096, vocab 4096), whose oracle answers tests/golden/tp_parity.npz holds
+PARITY_GEOM = dict(dim=1024, hidden_dim=4096, layers=2, heads=32, kv_heads=8, head_dim=128, vocab=4096, seq_len=64)
+
+
+def parity_check(rank, world, local, share_id, decode_kernels=0):
+    """Before anything is timed, at every GPU count: the tensor-parallel model over `world` ranks against the
+    oracle's answers (committed fixture).  fp32 mode: logits at the 8 prompt positions within 1e-3 relative
+    L2.  bf16 mode (the decode path the bench times): the oracle's 40 tokens fed one per step, every logits
+    row within 2e-2 relative L2 and every greedy choice after the prompt identical."""
+    import numpy as np
+    from common_b200 import native
+    fx = np.load(os.path.join(ROOT, "tests", "golden", "tp_parity.npz"))
+    g = PARITY_GEOM
+    seed, std = int(fx["seed"]), float(fx["std"])
+
+    def rel(a, b):
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+    out = {"fixture": "tests/golden/tp_parity.npz", "tp": world}
+    for prec, dt in (("fp32", native.DTYPE_F32), ("bf16", native.DTYPE_BF16)):
+        cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
+                                 g["vocab"], g["seq_len"], False, native.QKNORM_VECTOR, False, dt, dt, 1, 0,
+                                 decode_kernels=decode_kernels if prec == "bf16" else 0)
+        m = native.NativeModel(cfg, local, rank, world, share_id(native.unique_id))
+        m.init_synthetic(seed, std)
+        m.finalize()
+        if prec == "fp32":
+            errs = []
+            for p, t in enumerate(fx["prompt"]):
+                lg, _ = m.decode_step([int(t)], [p])
+                errs.append(rel(lg[0], fx["fp32_logits"][p]))
+            out["fp32_max_rel_l2"] = max(errs)
+        else:
+            toks, want = fx["bf16_tokens"], fx["bf16_logits"].astype(np.float32)
+            errs, bad = [], []
+            for p, t in enumerate(toks):
+                lg, am = m.decode_step([int(t)], [p])
+                errs.append(rel(lg[0], want[p]))
+                if p + 1 < len(toks) and p + 1 >= len(fx["prompt"]) and int(am[0]) != int(toks[p + 1]):
+                    bad.append(p + 1)
+            out["bf16_max_rel_l2"] = max(errs)
+            out["bf16_greedy_steps"] = len(toks) - len(fx["prompt"])
+            out["bf16_token_mismatches"] = bad
+            out["bf16_launches_per_token"] = m.last_launch_count
+        m.close()
+    out["ok"] = bool(out["fp32_max_rel_l2"] < 1e-3 and out["bf16_max_rel_l2"] < 2e-2 and not out["bf16_token_mismatches"])
+    return out
+
+
+# ----------------------------------------------------------------------------------- C2 / C5 decode legs
+GEOM_1P7B = dict(dim=2048, hidden_dim=6144, layers=28, heads=16, kv_heads=8, head_dim=128, vocab=151936,
+                 shared_weights=1, qk_norm=1, has_qkv_bias=0, rope_theta=1e6, eps=1e-6)
+GEOM_32B = dict(dim=5120, hidden_dim=25600, layers=64, heads=64, kv_heads=8, head_dim=128, vocab=151936,
+                shared_weights=0, qk_norm=1, has_qkv_bias=0, rope_theta=1e6, eps=1e-6)
+
+
+def run_decode_config(name, g, B, prompt_len, gen, rank, world, local, nid, peaks, chunk_tokens=32768):
+    """A batched greedy decode configuration: B sequences of uniform-random prompts prefilled on the tensor
+    cores (chunks of chunk_tokens), then `gen` batch-B decode steps captured as one CUDA graph step and
+    replayed (device-resident token feedback); tok/s = B * gen / the replay time (CUDA events, max over
+    ranks).  Roofline: HBM, bytes per step = every weight byte of the rank + the KV rows read."""
+    import numpy as np
+    import torch
+    from common_b200 import native
+    seq_len = prompt_len + gen + 8
+    per_chunk = max(1, min(B, chunk_tokens // prompt_len))
+    cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
+                             g["vocab"], seq_len, g["shared_weights"], native.QKNORM_VECTOR, False, native.DTYPE_BF16,
+                             native.DTYPE_BF16, B, per_chunk * prompt_len)
+    m = native.NativeModel(cfg, local, rank, world, nid)
+    m.init_synthetic(0, 0.02)
+    m.finalize()
+    stream = torch.cuda.ExternalStream(m.stream)
+    rng = np.random.default_rng(1)
+    prompts = rng.integers(0, g["vocab"], (B, prompt_len)).astype(np.int32)
+    first = np.zeros(B, np.int32)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for c0 in range(0, B, per_chunk):
+        sl = np.arange(c0, min(B, c0 + per_chunk), dtype=np.int32)
+        _, am = m.prefill(prompts[c0:c0 + per_chunk], slots=sl, want_logits=False)
+        first[c0:c0 + len(sl)] = am
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    for b in range(B):
+        m.reserve(b, seq_len)
+    dt = torch.tensor(first, dtype=torch.int32, device="cuda")
+    dp = torch.full((B,), prompt_len, dtype=torch.int32, device="cuda")
+    ds = torch.arange(B, dtype=torch.int32, device="cuda")
+    dam = torch.zeros(B, dtype=torch.int32, device="cuda")
+    m.capture_decode(dt.data_ptr(), ds.data_ptr(), dp.data_ptr(), B, 0, dam.data_ptr())
+    launches = m.last_launch_count
+    warm = 3
+    m.replay_decode(warm)
+    m.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    m.replay_decode(gen - warm)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    m.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    steps = gen - warm
+    ctx_mid = prompt_len + warm + steps // 2
+    wb = weight_bytes(g, world)
+    step_bytes = wb["layers_total"] + wb["lm_head"] + B * kv_bytes_per_token(g, ctx_mid, world)
+    gbs = step_bytes / (ms / steps * 1e-3) / 1e9
+    peak = peaks.get("hbm_gbs", 6650.0)
+    m.close()
+    return {"workload": name, "tok_s": B * steps / (ms * 1e-3), "ms_per_step": ms / steps, "batch": B,
+            "prompt_len": prompt_len, "generated": gen, "timed_steps": steps, "warmup_steps": warm,
+            "context": [prompt_len + warm, prompt_len + gen], "launches_per_step": launches, "parallelism": f"tp{world}",
+            "prefill_s": prefill_s,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "bytes_per_step": step_bytes, "per": "GPU" if world == 1 else "rank"}}
+
+
 # ----------------------------------------------------------------------------------- GPU arm
 def run_ours(args):
     import numpy as np
@@ -250,6 +390,9 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     build.build()
     from common_b200 import parallel
+    parity = parity_check(rank, world, local, parallel.share_unique_id, args.decode_kernels)
+    if not parity["ok"]:
+        print(json.dumps({"parity_failed": parity}), file=sys.stderr, flush=True)
     nid = parallel.share_unique_id(native.unique_id)  # one NCCL id per communicator (per model)
     g = GEOM_8B
     B = 1
@@ -257,7 +400,8 @@ def run_ours(args):
     seq_len = PROMPT + args.warmup + args.steps + e2e_steps + 8
     cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
                              g["vocab"], seq_len, False, native.QKNORM_VECTOR, False, native.DTYPE_BF16,
-                             native.DTYPE_BF16, B, PROMPT)  # the prompt is one tensor-core prefill chunk
+                             native.DTYPE_BF16, B, PROMPT,  # the prompt is one tensor-core prefill chunk
+                             decode_kernels=args.decode_kernels)
     m = native.NativeModel(cfg, local, rank, world, nid)
     m.init_synthetic(0, 0.02)
     m.finalize()
@@ -356,16 +500,27 @@ def run_ours(args):
 
     m.close()
     torch.cuda.empty_cache()
+    extra = {}
+    if world == 1 and not args.no_configs:
+        extra["c2_decode_b16"] = run_decode_config(
+            "qwen3-1.7b batch-16 decode, 2048-token prompts, 128 generated (BASELINE configs[1])", GEOM_1P7B, 16, 2048,
+            128, rank, world, local, None, peaks_of())
+        torch.cuda.empty_cache()
+    if world == 8 and not args.no_configs:
+        extra["c5_decode_b64"] = run_decode_config(
+            "qwen3-32b tp8 batch-64 decode, paged KV at 8192 context, 128 generated (BASELINE configs[4])", GEOM_32B,
+            64, 8192, 128, rank, world, local, parallel.share_unique_id(native.unique_id), peaks_of())
+        torch.cuda.empty_cache()
     batched = None
     if not args.no_batched:
         batched = run_batched(args, rank, world, local, parallel.share_unique_id(native.unique_id), peaks)
         torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tok_s, dts, cores = cpu_sample(args.cpu_samples, 2)
+        tok_s, dts, cores = cpu_sample(args.cpu_tokens, 2)
         cpu = {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port",
-               "sample": f"oracle port fp32 at the 8B geometry (layer weights shared), {args.cpu_samples} samples of "
-                         f"one layer + 1/36 lm_head at context {PROMPT} = {args.cpu_samples / 36:.2f} tokens, {dts:.1f} s"}
+               "sample": f"oracle port fp32 at the 8B geometry (layer weights shared), {args.cpu_tokens} whole decode "
+                         f"tokens (36 layers + full lm_head) at context {PROMPT}, {dts:.1f} s"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -383,8 +538,10 @@ def run_ours(args):
                              "step_gbs": step_gbs, "step_frac": step_gbs / peak},
                 "kernel_ms_per_step": tot, "gpu_launches": launches_per_step * args.steps,
                 "launches_per_step": launches_per_step, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu}
+        line["parity"] = parity
         if batched:
             line.update(batched)
+        line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -456,7 +613,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=64)
-    ap.add_argument("--cpu-samples", type=int, default=1080)
+    ap.add_argument("--cpu-tokens", type=int, default=30, help="whole tokens of the CPU baseline leg")
     ap.add_argument("--no-batched", action="store_true", help="skip the prefill / batch-64 decode measurements")
     ap.add_argument("--prefill-seqs", type=int, default=8)
     ap.add_argument("--prefill-len", type=int, default=4096)
@@ -467,6 +624,9 @@ def main():
     ap.add_argument("--layers", type=int, default=4, help="--case step-small: layers of the cut 8B model")
     ap.add_argument("--gemm", type=int, nargs=4, default=[24576, 4096, 4096, 2], metavar=("M", "K", "T", "EPI"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[1] (1 GPU) / configs[4] (8 GPUs) legs")
+    ap.add_argument("--decode-kernels", type=int, default=0,
+                    help="batch-1 decode path: 0 auto, 1 one kernel per operation, 2 the persistent step kernel")
     ap.add_argument("--prompt-len", type=int, default=PROMPT, help="shorter prompts for profiler runs")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -78,7 +78,7 @@ __device__ __forceinline__ void attn_issue(typename KVec<KT, DPL>::T (&kr)[kAttn
 }
 
 template <typename KT, int D, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32) qw_attn_decode_kernel(const AttnArgs a) {
     constexpr int DPL = D / 32;
     constexpr int HALF = D / 2;
     constexpr int TILE = kAttnWarps * kAttnTPW;
@@ -347,10 +347,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 template <typename KT, int D>
 static cudaError_t attn_launch_g(const AttnArgs &a, int G, dim3 grid, cudaStream_t st) {
     switch (G) {
-        case 1: attn_decode_kernel<KT, D, 1><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
-        case 2: attn_decode_kernel<KT, D, 2><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
-        case 4: attn_decode_kernel<KT, D, 4><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
-        case 8: attn_decode_kernel<KT, D, 8><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
+        case 1: qw_attn_decode_kernel<KT, D, 1><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
+        case 2: qw_attn_decode_kernel<KT, D, 2><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
+        case 4: qw_attn_decode_kernel<KT, D, 4><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
+        case 8: qw_attn_decode_kernel<KT, D, 8><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

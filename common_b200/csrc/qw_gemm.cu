@@ -164,7 +164,7 @@ __device__ __forceinline__ TileCoord tile_coord(int tile, int nf, int nt, int nk
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
+    qw_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
     constexpr int S = tc_stages(BN);
     constexpr int A_BYTES = kBM * kBK * 2, B_BYTES = BN * kBK * 2;
     constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -414,7 +414,7 @@ cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int cols, int b
 
 template <int BN, int EPI>
 cudaError_t launch_bn(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a, int num_sms, cudaStream_t st) {
-    auto kfn = tc_gemm_kernel<BN, EPI>;
+    auto kfn = qw_tc_gemm_kernel<BN, EPI>;
     const int nf = (a.M + kBM - 1) / kBM, nt = (a.T + BN - 1) / BN;
     const int total = nf * nt * a.ksplit;
     const int grid = total < num_sms ? total : num_sms;
@@ -435,11 +435,11 @@ cudaError_t launch_epi(const CUtensorMap &mw, const CUtensorMap &mx, const TcArg
 }  // namespace
 
 cudaError_t tc_prepare() {
-    const void *fns[] = {(const void *)tc_gemm_kernel<64, TC_STORE>,  (const void *)tc_gemm_kernel<128, TC_STORE>,
-                         (const void *)tc_gemm_kernel<256, TC_STORE>, (const void *)tc_gemm_kernel<64, TC_RESID>,
-                         (const void *)tc_gemm_kernel<128, TC_RESID>, (const void *)tc_gemm_kernel<256, TC_RESID>,
-                         (const void *)tc_gemm_kernel<64, TC_SWIGLU>, (const void *)tc_gemm_kernel<128, TC_SWIGLU>,
-                         (const void *)tc_gemm_kernel<256, TC_SWIGLU>};
+    const void *fns[] = {(const void *)qw_tc_gemm_kernel<64, TC_STORE>,  (const void *)qw_tc_gemm_kernel<128, TC_STORE>,
+                         (const void *)qw_tc_gemm_kernel<256, TC_STORE>, (const void *)qw_tc_gemm_kernel<64, TC_RESID>,
+                         (const void *)qw_tc_gemm_kernel<128, TC_RESID>, (const void *)qw_tc_gemm_kernel<256, TC_RESID>,
+                         (const void *)qw_tc_gemm_kernel<64, TC_SWIGLU>, (const void *)qw_tc_gemm_kernel<128, TC_SWIGLU>,
+                         (const void *)qw_tc_gemm_kernel<256, TC_SWIGLU>};
     const int bns[] = {64, 128, 256, 64, 128, 256, 64, 128, 256};
     for (int i = 0; i < 9; i++) {
         cudaError_t e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes(bns[i]));

@@ -86,7 +86,7 @@ __device__ __forceinline__ void gemv_issue(uint4 (&u)[kGemvRows][kGemvUnroll], c
 // buffer), the first stage is issued before the programmatic-launch wait so it overlaps the
 // previous kernel's tail, and partial sums meet in shared memory once per tile.
 template <typename WT, int EPI, int NB>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads) qw_gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(16) float xs[];  // [NB][K]
     __shared__ float red[2][kGemvWarps][kGemvRows * NB];
     __shared__ float am_v[kGemvRows * NB];
@@ -331,7 +331,7 @@ static int prepare_cached(const void *fn, size_t smem, cudaError_t *err) {
 template <typename WT, int EPI, int NB>
 static cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t st) {
     size_t smem = (size_t)NB * a.K * sizeof(float);
-    auto kfn = gemv_kernel<WT, EPI, NB>;
+    auto kfn = qw_gemv_kernel<WT, EPI, NB>;
     cudaError_t e = cudaSuccess;
     int occ = prepare_cached((const void *)kfn, smem, &e);
     if (e != cudaSuccess) return e;

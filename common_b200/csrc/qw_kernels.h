@@ -183,6 +183,8 @@ struct StepArgs {
     int kv_bf16;
     unsigned long long *trace;       // optional: CTA 0's globaltimer before / after every grid barrier
     int evict_first;                 // weight stream marked L2 evict-first (keeps code, KV and activations resident)
+    unsigned long long wait_cycles;  // bound of every wait in SM clock cycles; on expiry the kernel reports and returns
+    int stall_cta;                   // test hook (-1 = off): this CTA withholds its arrival at the step's first barrier
 };
 
 size_t step_smem_bytes(const StepArgs &a);

@@ -10,7 +10,7 @@ namespace qw {
 // dst[map(r) * ld + c] = convert(src[r * src_ld + c])  or the synthetic value of the full
 // tensor's element (src_row0 + r, src_col0 + c).
 template <typename DT>
-__global__ void place_kernel(const PlaceArgs p) {
+__global__ void qw_place_kernel(const PlaceArgs p) {
     const size_t total = (size_t)p.rows * p.cols;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         int r = (int)(i / p.cols), c = (int)(i % p.cols);
@@ -39,14 +39,14 @@ cudaError_t place_launch(const PlaceArgs &p, cudaStream_t st) {
     if (!total) return cudaSuccess;
     int grid = (int)((total + 255) / 256);
     if (grid > 148 * 16) grid = 148 * 16;
-    if (p.dst_bf16) place_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
-    else place_kernel<float><<<grid, 256, 0, st>>>(p);
+    if (p.dst_bf16) qw_place_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else qw_place_kernel<float><<<grid, 256, 0, st>>>(p);
     return cudaGetLastError();
 }
 
 // freq[p][f] = (cos, sin)(p * exp(-2 f ln(theta) / d)), computed in fp64 like the reference's
 // default precision (RotationFeatures.java:189-208), stored as fp32.
-__global__ void freq_kernel(float2 *freq, int seq_len, int half, double neg2lt_over_d) {
+__global__ void qw_freq_kernel(float2 *freq, int seq_len, int half, double neg2lt_over_d) {
     size_t total = (size_t)seq_len * half;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         int p = (int)(i / half), f = (int)(i % half);
@@ -61,12 +61,12 @@ cudaError_t freq_launch(float2 *freq, int seq_len, int head_dim, double theta, c
     size_t total = (size_t)seq_len * half;
     int grid = (int)((total + 255) / 256);
     if (grid > 148 * 8) grid = 148 * 8;
-    freq_kernel<<<grid, 256, 0, st>>>(freq, seq_len, half, -2.0 * log(theta) / head_dim);
+    qw_freq_kernel<<<grid, 256, 0, st>>>(freq, seq_len, half, -2.0 * log(theta) / head_dim);
     return cudaGetLastError();
 }
 
 // Cross-rank greedy pick: (val, idx) gathered from every rank -> winner (ties -> smaller index).
-__global__ void argmax_merge_kernel(const float *vals, const int *idxs, int tp, int B, int *argmax_out,
+__global__ void qw_argmax_merge_kernel(const float *vals, const int *idxs, int tp, int B, int *argmax_out,
                                     int *next_tokens, int *positions, int advance, int *hist, int hist_ld) {
     int b = threadIdx.x;
     if (b >= B) return;
@@ -87,14 +87,14 @@ __global__ void argmax_merge_kernel(const float *vals, const int *idxs, int tp, 
 
 cudaError_t argmax_merge_launch(const float *vals, const int *idxs, int tp, int B, int *argmax_out, int *next_tokens,
                                 int *positions, int advance, int *hist, int hist_ld, cudaStream_t st) {
-    argmax_merge_kernel<<<1, 32 * ((B + 31) / 32), 0, st>>>(vals, idxs, tp, B, argmax_out, next_tokens, positions, advance,
+    qw_argmax_merge_kernel<<<1, 32 * ((B + 31) / 32), 0, st>>>(vals, idxs, tp, B, argmax_out, next_tokens, positions, advance,
                                                             hist, hist_ld);
     return cudaGetLastError();
 }
 
 // Per-rank sums of squares of the local q and k slices (whole-vector QK-norm under tensor
 // parallelism; the caller all-reduces them).  out: (B, 2).
-__global__ void qk_sumsq_kernel(const float *qkv, int ld, int qw, int kw, float *out) {
+__global__ void qw_qk_sumsq_kernel(const float *qkv, int ld, int qw, int kw, float *out) {
     int b = blockIdx.x;
     const float *row = qkv + (size_t)b * ld;
     float sq = 0.f, sk = 0.f;
@@ -115,12 +115,12 @@ __global__ void qk_sumsq_kernel(const float *qkv, int ld, int qw, int kw, float 
 }
 
 cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, float *out, cudaStream_t st) {
-    qk_sumsq_kernel<<<B, 256, 0, st>>>(qkv, ld, qw, kw, out);
+    qw_qk_sumsq_kernel<<<B, 256, 0, st>>>(qkv, ld, qw, kw, out);
     return cudaGetLastError();
 }
 
 // x_out = x_in + part (residual after a tensor-parallel all-reduce), rows x n
-__global__ void add_kernel(float *out, const float *a, const float *b, size_t n) {
+__global__ void qw_add_kernel(float *out, const float *a, const float *b, size_t n) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = a[i] + b[i];
 }
@@ -128,13 +128,13 @@ cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cud
     int grid = (int)((n + 255) / 256);
     if (grid > 148 * 8) grid = 148 * 8;
     if (grid < 1) grid = 1;
-    add_kernel<<<grid, 256, 0, st>>>(out, a, b, n);
+    qw_add_kernel<<<grid, 256, 0, st>>>(out, a, b, n);
     return cudaGetLastError();
 }
 
 // out[0, n) = 0 inside a chain of programmatically launched kernels (a memset node would end the
 // chain): the accumulator of a split-K GEMM that follows.
-__global__ void zero_kernel(float4 *out, size_t n4) {
+__global__ void qw_zero_kernel(float4 *out, size_t n4) {
     griddep_launch_dependents();
     griddep_wait();  // the previous kernel may still read the buffer
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
@@ -145,12 +145,12 @@ cudaError_t zero_launch(float *out, size_t n, cudaStream_t st) {
     int grid = (int)((n / 4 + 255) / 256);
     if (grid > 148 * 4) grid = 148 * 4;
     if (grid < 1) grid = 1;
-    return launch_pdl(zero_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<float4 *>(out), n / 4);
+    return launch_pdl(qw_zero_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<float4 *>(out), n / 4);
 }
 
 // h[t][p] = up * silu(gate) for rows of the (2F) gate/up projection interleaved in blocks of 16 gate then 16 up
 // rows, as the GEMM's SwiGLU epilogue computes it (same expression), h bf16 (T, F).
-__global__ void swiglu_rows_kernel(const float *gu, int F, __nv_bfloat16 *h) {
+__global__ void qw_swiglu_rows_kernel(const float *gu, int F, __nv_bfloat16 *h) {
     griddep_launch_dependents();
     griddep_wait();
     const int t = blockIdx.y;
@@ -164,12 +164,12 @@ __global__ void swiglu_rows_kernel(const float *gu, int F, __nv_bfloat16 *h) {
 cudaError_t swiglu_rows_launch(const float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st) {
     if (T < 1 || F < 1) return cudaErrorInvalidValue;
     const int bx = (F + 255) / 256 < 8 ? (F + 255) / 256 : 8;
-    return launch_pdl(swiglu_rows_kernel, dim3(bx, T), dim3(256), 0, st, gu, F, h);
+    return launch_pdl(qw_swiglu_rows_kernel, dim3(bx, T), dim3(256), 0, st, gu, F, h);
 }
 
 // Bounded busy-wait of `ns` nanoseconds on the device (globaltimer), used to let the host
 // run ahead of the GPU before a profiled sequence of launches.  Ends by itself.
-__global__ void hold_kernel(unsigned long long ns) {
+__global__ void qw_hold_kernel(unsigned long long ns) {
     unsigned long long t0, t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     for (int i = 0; i < (1 << 24); i++) {
@@ -179,7 +179,7 @@ __global__ void hold_kernel(unsigned long long ns) {
     }
 }
 cudaError_t hold_launch(unsigned long long ns, cudaStream_t st) {
-    hold_kernel<<<1, 32, 0, st>>>(ns);
+    qw_hold_kernel<<<1, 32, 0, st>>>(ns);
     return cudaGetLastError();
 }
 

@@ -418,14 +418,20 @@ qw_status decode_pass(qw_model *m, const int *tokens, const float *x_in, const i
     const bool tpm = m->tp > 1;
     float *xcur = m->xa, *xalt = m->xb;
     const float *pending = nullptr;  // all-reduced partial to be added to xcur (tp > 1)
-    if (B == 1 && tokens && !x_in && m->use_step && (m->tp == 1 || !logits_out_dev)) {
+    if (B == 1 && tokens && !x_in && m->use_step) {
         StepArgs sa = m->step;
         sa.tokens = next_tokens ? next_tokens : const_cast<int *>(tokens);
         sa.positions = positions; sa.slots = slots; sa.advance = advance; sa.hist = hist;
-        sa.argmax_out = argmax_dev; sa.logits = logits_out_dev;
+        // under tensor parallelism every rank writes its vocabulary shard, gathered below
+        sa.argmax_out = argmax_dev; sa.logits = tpm && logits_out_dev ? m->logits : logits_out_dev;
         sa.trace = m->prof_on ? m->d_trace : nullptr;
         CK(cudaMemsetAsync(sa.bar, 0, sizeof(unsigned) * m->step_zero_words, m->st));
         LKK(QW_KERNEL_STEP, step_launch(sa, m->bf16kv, m->num_sms, m->st));
+        if (tpm && logits_out_dev) {
+            NK(ncclAllGather(m->logits, m->logits_all, (size_t)m->Vl, ncclFloat, m->comm, m->st));
+            CK(cudaMemcpyAsync(logits_out_dev, m->logits_all, sizeof(float) * m->c.vocab, cudaMemcpyDeviceToDevice,
+                               m->st));
+        }
         return QW_OK;
     }
     int nsplit = choose_nsplit(m, B);
@@ -1004,6 +1010,13 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 {
                     const char *ev = getenv("QW_STEP_EVICT");
                     sa.evict_first = ev ? atoi(ev) : 1;
+                }
+                {
+                    int khz = 0;
+                    CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device));
+                    const long long us = c.wait_limit_us > 0 ? c.wait_limit_us : 2000000;
+                    sa.wait_cycles = (unsigned long long)us * (unsigned long long)(khz > 0 ? khz : 2000000) / 1000ull;
+                    sa.stall_cta = c.test_stall_cta > 0 ? c.test_stall_cta - 1 : -1;
                 }
                 sa.tp = tp_size; sa.rank = tp_rank; sa.v0 = m->v0;
                 sa.q_total = c.heads * c.head_dim; sa.kv_total = c.kv_heads * c.head_dim;

@@ -24,7 +24,7 @@ namespace qw {
 constexpr int kNormThreads = 256;
 constexpr size_t kPrepSmem = 160 * 1024;  // dynamic shared memory the row kernels are opted in to
 
-__global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(NormRowsArgs a) {
+__global__ void __launch_bounds__(kNormThreads) qw_norm_rows_kernel(NormRowsArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
     griddep_wait();               // the previous kernel's results
     extern __shared__ __align__(16) float xrow[];
@@ -69,7 +69,7 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
     if (rows < 1 || a.K % 4) return cudaErrorInvalidValue;
     size_t smem = sizeof(float) * a.K;
     if (smem > kPrepSmem) return cudaErrorInvalidValue;
-    return launch_pdl(norm_rows_kernel, dim3(rows), dim3(kNormThreads), smem, st, a);
+    return launch_pdl(qw_norm_rows_kernel, dim3(rows), dim3(kNormThreads), smem, st, a);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -78,7 +78,7 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
 constexpr int kPostThreads = 256;
 
 template <typename KT>
-__global__ void __launch_bounds__(kPostThreads) qkv_post_kernel(QkvPostArgs a) {
+__global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
     griddep_wait();               // the previous kernel's results
     extern __shared__ __align__(16) float row[];  // q (Ql) | k (KVl) | v (KVl)
@@ -150,8 +150,8 @@ __global__ void __launch_bounds__(kPostThreads) qkv_post_kernel(QkvPostArgs a) {
 
 cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st) {
     size_t smem = sizeof(float) * (size_t)(a.H + 2 * a.Hkv) * a.d;
-    auto k16 = qkv_post_kernel<__nv_bfloat16>;
-    auto k32 = qkv_post_kernel<float>;
+    auto k16 = qw_qkv_post_kernel<__nv_bfloat16>;
+    auto k32 = qw_qkv_post_kernel<float>;
     if (smem > kPrepSmem) return cudaErrorInvalidValue;
     return kv_bf16 ? launch_pdl(k16, dim3(rows), dim3(kPostThreads), smem, st, a)
                    : launch_pdl(k32, dim3(rows), dim3(kPostThreads), smem, st, a);
@@ -200,7 +200,7 @@ __device__ __forceinline__ uint32_t fa_off(int row, int chunk) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kFaWarps * 32) flash_prefill_kernel(FlashArgs a) {
+__global__ void __launch_bounds__(kFaWarps * 32) qw_flash_prefill_kernel(FlashArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
     griddep_wait();               // the previous kernel's results
     constexpr int CH = D / 8;  // 16-byte chunks per row
@@ -361,9 +361,9 @@ cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st) 
     dim3 grid((a.L + kFaRows - 1) / kFaRows, a.H, nseq);
     if (a.d == 128) {
         const size_t smem = 4 * kFaKeys * 128 * 2;
-        return launch_pdl(flash_prefill_kernel<128>, grid, dim3(kFaWarps * 32), smem, st, a);
+        return launch_pdl(qw_flash_prefill_kernel<128>, grid, dim3(kFaWarps * 32), smem, st, a);
     }
-    if (a.d == 64) return launch_pdl(flash_prefill_kernel<64>, grid, dim3(kFaWarps * 32), 4 * kFaKeys * 64 * 2, st, a);
+    if (a.d == 64) return launch_pdl(qw_flash_prefill_kernel<64>, grid, dim3(kFaWarps * 32), 4 * kFaKeys * 64 * 2, st, a);
     return cudaErrorInvalidValue;
 }
 
@@ -377,7 +377,7 @@ cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st) 
 constexpr int kFdStages = 3;
 
 template <int D, int G>
-__global__ void __launch_bounds__(kFaWarps * 32) flash_decode_kernel(FlashDecodeArgs a) {
+__global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDecodeArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
     griddep_wait();               // the previous kernel's results
     constexpr int CH = D / 8;
@@ -587,10 +587,10 @@ static cudaError_t flash_decode_g(const FlashDecodeArgs &a, dim3 grid, cudaStrea
     const size_t smem = (size_t)kFdStages * 2 * kFaKeys * D * 2;
     const dim3 block(kFaWarps * 32);
     switch (a.H / a.Hkv) {
-        case 1: return launch_pdl(flash_decode_kernel<D, 1>, grid, block, smem, st, a);
-        case 2: return launch_pdl(flash_decode_kernel<D, 2>, grid, block, smem, st, a);
-        case 4: return launch_pdl(flash_decode_kernel<D, 4>, grid, block, smem, st, a);
-        case 8: return launch_pdl(flash_decode_kernel<D, 8>, grid, block, smem, st, a);
+        case 1: return launch_pdl(qw_flash_decode_kernel<D, 1>, grid, block, smem, st, a);
+        case 2: return launch_pdl(qw_flash_decode_kernel<D, 2>, grid, block, smem, st, a);
+        case 4: return launch_pdl(qw_flash_decode_kernel<D, 4>, grid, block, smem, st, a);
+        case 8: return launch_pdl(qw_flash_decode_kernel<D, 8>, grid, block, smem, st, a);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -606,7 +606,7 @@ cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st
 // ------------------------------------------------------------------------------------------
 // rows_argmax: one CTA per logits row; first index of the maximum
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) rows_argmax_kernel(RowsArgmaxArgs a) {
+__global__ void __launch_bounds__(512) qw_rows_argmax_kernel(RowsArgmaxArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
     griddep_wait();               // the previous kernel's results
     __shared__ float sv[16];
@@ -643,13 +643,13 @@ __global__ void __launch_bounds__(512) rows_argmax_kernel(RowsArgmaxArgs a) {
 }
 
 cudaError_t prefill_kernels_prepare() {
-    const void *fns[] = {(const void *)norm_rows_kernel, (const void *)qkv_post_kernel<__nv_bfloat16>,
-                         (const void *)qkv_post_kernel<float>, (const void *)flash_prefill_kernel<128>,
-                         (const void *)flash_prefill_kernel<64>,
-                         (const void *)flash_decode_kernel<128, 1>, (const void *)flash_decode_kernel<128, 2>,
-                         (const void *)flash_decode_kernel<128, 4>, (const void *)flash_decode_kernel<128, 8>,
-                         (const void *)flash_decode_kernel<64, 1>, (const void *)flash_decode_kernel<64, 2>,
-                         (const void *)flash_decode_kernel<64, 4>, (const void *)flash_decode_kernel<64, 8>};
+    const void *fns[] = {(const void *)qw_norm_rows_kernel, (const void *)qw_qkv_post_kernel<__nv_bfloat16>,
+                         (const void *)qw_qkv_post_kernel<float>, (const void *)qw_flash_prefill_kernel<128>,
+                         (const void *)qw_flash_prefill_kernel<64>,
+                         (const void *)qw_flash_decode_kernel<128, 1>, (const void *)qw_flash_decode_kernel<128, 2>,
+                         (const void *)qw_flash_decode_kernel<128, 4>, (const void *)qw_flash_decode_kernel<128, 8>,
+                         (const void *)qw_flash_decode_kernel<64, 1>, (const void *)qw_flash_decode_kernel<64, 2>,
+                         (const void *)qw_flash_decode_kernel<64, 4>, (const void *)qw_flash_decode_kernel<64, 8>};
     for (const void *f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
         if (e != cudaSuccess) return e;
@@ -658,7 +658,7 @@ cudaError_t prefill_kernels_prepare() {
 }
 
 cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t st) {
-    return launch_pdl(rows_argmax_kernel, dim3(rows), dim3(512), 0, st, a);
+    return launch_pdl(qw_rows_argmax_kernel, dim3(rows), dim3(512), 0, st, a);
 }
 
 }  // namespace qw

@@ -60,7 +60,7 @@ __device__ __forceinline__ double jr_next_double(unsigned long long &seed) {
     return (double)((hi << 27) + lo) * (1.0 / 9007199254740992.0);
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_rows_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kSampThreads) qw_sample_rows_kernel(SampleArgs a) {
     __shared__ double red[kSampWarps];
     __shared__ double hist_m[2048];
     __shared__ int s_pick;
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_rows_kernel(SampleArgs a)
 
 cudaError_t sample_rows_launch(const SampleArgs &a, int rows, cudaStream_t st) {
     if (rows < 1 || a.V < 1) return cudaErrorInvalidValue;
-    sample_rows_kernel<<<rows, kSampThreads, 0, st>>>(a);
+    qw_sample_rows_kernel<<<rows, kSampThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -40,13 +40,11 @@ constexpr int kStepConsumerWarps = 8;
 constexpr int kStepConsumers = kStepConsumerWarps * 32;
 constexpr int kStepThreads = kStepConsumers + 32;
 static_assert(kStepThreads == kStepBlockThreads, "block size");
-constexpr int kRows = 4;        // weight rows per ring slot
-constexpr int kPiece = 32768;  // bytes per ring slot (kRows rows x up to 4096 columns)
+constexpr int kPiece = 32768;  // bytes per ring slot (16384 bf16 weights: R rows x C columns)
 constexpr int kRing = 5;
-constexpr unsigned long long kStepWaitNs = 4000ull * 1000ull * 1000ull;  // cycles: ~2 s at 2 GHz
 // layout of a rank's exchange buffer (32-bit words): flags, QK-norm sums, argmax, row partials
 constexpr int kXFlags = 0;   // [tp] generation flags, written by each peer
-constexpr int kXSs = 64;     // [2][2] q / k sums of squares accumulated over all ranks (even / odd layers)
+constexpr int kXSs = 64;     // [tp][2] q / k sums of squares of the current layer, one slot per rank
 constexpr int kXAm = 96;     // [tp][2] (value, index) of each rank's vocabulary shard
 constexpr int kXRows = 128;  // [2][tp][D]: O partials, then down partials
 constexpr int kStepTPW = 4;  // attention: keys per warp per tile (small: this code runs once per layer, cold in the instruction cache)
@@ -69,14 +67,15 @@ __device__ __forceinline__ bool mb_try(uint32_t addr, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
+__device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err,
+                                        unsigned long long lim) {
     const uint32_t addr = su32(b);
     if (mb_try(addr, parity)) return true;
     const uint64_t t0 = now_ns();
     for (;;) {
         if (mb_try(addr, parity)) return true;
         if (*abort_flag) return false;
-        if (now_ns() - t0 > kStepWaitNs) {
+        if (now_ns() - t0 > lim) {
             *abort_flag = 1;
             atomicExch(err, 1);
             return false;
@@ -111,32 +110,39 @@ struct Ring {
     uint8_t *buf;
     int slot;
     uint32_t ph;
+    unsigned long long lim;  // wait bound (cycles)
 };
 
-// Column chunk of one ring slot: a slot holds the same C columns of kRows consecutive rows, so every
-// activation value read from shared memory serves kRows weight rows.
+// Column chunk of one ring slot.  A slot holds the same C columns of R = 16384 / C consecutive rows
+// (32 KiB of bf16): wide matrices fill a slot with 4 rows of 4096 columns, the narrow K of a
+// tensor-parallel shard (K = 512 at tp 8) with 32 rows of 512, so that every slot carries the same bytes
+// whatever the shard.  Every activation value read from shared memory serves 4 weight rows.
 __host__ __device__ __forceinline__ int chunk_cols(int K) {
     return (K & 4095) == 0 ? 4096 : ((K & 2047) == 0 ? 2048 : ((K & 1023) == 0 ? 1024 : 512));
 }
+__host__ __device__ __forceinline__ int slot_rows(int C) { return (kPiece / 2) / C; }
 
-// producer: this CTA's rows [r0, r1) of W (N, K), kRows rows at a time, each group in column chunks
+// producer: this CTA's rows [r0, r1) of W (N, K), R rows at a time, each group in column chunks.  When a
+// chunk spans whole rows (K == C) the group is one contiguous copy.
 __device__ __forceinline__ bool produce(Ring &rg, const __nv_bfloat16 *W, int N, int K, volatile int *abort_flag,
                                         int *err, uint32_t &issued, uint32_t &last_ph, uint64_t policy) {
     int r0, r1;
     split_rows(N, blockIdx.x, gridDim.x, r0, r1);
-    const int C = chunk_cols(K);
-    for (int ra = r0; ra < r1; ra += kRows) {
-        const int nr = min(kRows, r1 - ra);
+    const int C = chunk_cols(K), R = slot_rows(C);
+    for (int ra = r0; ra < r1; ra += R) {
+        const int nr = min(R, r1 - ra);
         for (int c0 = 0; c0 < K; c0 += C) {
-            if (!mb_wait(&rg.empty[rg.slot], rg.ph ^ 1u, abort_flag, err)) return false;
+            if (!mb_wait(&rg.empty[rg.slot], rg.ph ^ 1u, abort_flag, err, rg.lim)) return false;
             const uint32_t fb = su32(&rg.full[rg.slot]);
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb), "r"((uint32_t)(nr * C * 2))
                          : "memory");
-            for (int j = 0; j < nr; j++)
+            const int ncopy = C == K ? 1 : nr;
+            const uint32_t bytes = (uint32_t)((C == K ? nr : 1) * C * 2);
+            for (int j = 0; j < ncopy; j++)
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
                     "%4;" ::"r"(su32(rg.buf + (size_t)rg.slot * kPiece + (size_t)j * C * 2)),
-                    "l"(W + (size_t)(ra + j) * K + c0), "r"((uint32_t)(C * 2)), "r"(fb), "l"(policy)
+                    "l"(W + (size_t)(ra + j) * K + c0), "r"(bytes), "r"(fb), "l"(policy)
                     : "memory");
             issued |= 1u << rg.slot;
             last_ph = (last_ph & ~(1u << rg.slot)) | (rg.ph << rg.slot);
@@ -171,88 +177,66 @@ __device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v
     return z;
 }
 
-// consumers: acc[r - r0] = W[r, :] . xs for this CTA's rows; returns the row range.  Warp w takes
-// columns [w C/8, (w+1) C/8) of each slot in 128-column steps, lane l columns 4l .. 4l+3 of a step
-// (contiguous 16-byte activation loads, 8-byte weight loads), for all kRows rows of the slot; the
-// partial sums stay in registers until the row group is done.  C is a template argument so the
-// slot loop unrolls completely.
+// consumers: acc[r - r0] = W[r, :] . xs for this CTA's rows.  Every warp takes a 4-row x 512-column block of
+// each slot (row block w / (C / 512), column block w % (C / 512)) in 128-column steps, lane l columns
+// 4l .. 4l+3 of a step (contiguous 16-byte activation loads, 8-byte weight loads); the partial sums stay in
+// registers until the row group is done.  C is a template argument so the slot loop unrolls completely.
 template <int C>
 __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
                                           volatile int *abort_flag, int *err) {
-    constexpr int PER_WARP = C / 8;
-    constexpr int STEPS = PER_WARP / 128;
-    static_assert(STEPS >= 1, "C >= 1024 (see consume_512)");
-    static_assert(kRows == 4, "warp_sum4 reduces four rows");
+    constexpr int CB = C / 512;          // column blocks per slot
+    constexpr int R = (kPiece / 2) / C;  // rows per slot
+    constexpr int STEPS = 4;
+    static_assert(R == 4 * (kStepConsumerWarps / CB), "8 warps cover a slot");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cw = warp * PER_WARP + lane * 4;
-    for (int ra = r0; ra < r1; ra += kRows) {
-        const int nr = min(kRows, r1 - ra);
-        float p[kRows][STEPS];
+    const int rb = (warp / CB) * 4, cw = (warp % CB) * 512 + lane * 4;
+    for (int ra = r0; ra < r1; ra += R) {
+        const int nr = min(R, r1 - ra) - rb;  // rows of this warp's block present in the group (may be <= 0)
+        float p[4][STEPS];
 #pragma unroll
-        for (int r = 0; r < kRows; r++)
+        for (int r = 0; r < 4; r++)
 #pragma unroll
             for (int j = 0; j < STEPS; j++) p[r][j] = 0.f;
         for (int c0 = 0; c0 < K; c0 += C) {
-            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err)) return false;
-            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
-            const float *xp = xs + c0 + cw;
-            float4 x[STEPS];
-            uint2 w[kRows][STEPS];
+            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err, rg.lim)) return false;
+            if (nr > 0) {
+                const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + ((size_t)rb * C + cw) * 2;
+                const float *xp = xs + c0 + cw;
+                float4 x[STEPS];
+                uint2 w[4][STEPS];
 #pragma unroll
-            for (int j = 0; j < STEPS; j++) {
-                x[j] = *reinterpret_cast<const float4 *>(xp + j * 128);
+                for (int j = 0; j < STEPS; j++) {
+                    x[j] = *reinterpret_cast<const float4 *>(xp + j * 128);
 #pragma unroll
-                for (int r = 0; r < kRows; r++)
-                    w[r][j] = *reinterpret_cast<const uint2 *>(sa + (size_t)r * C * 2 + j * 256);
-            }
-            __syncwarp();
-            if (lane == 0)
+                    for (int r = 0; r < 4; r++)
+                        w[r][j] = *reinterpret_cast<const uint2 *>(sa + (size_t)r * C * 2 + j * 256);
+                }
+                __syncwarp();
+                if (lane == 0)
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+#pragma unroll
+                for (int j = 0; j < STEPS; j++)
+#pragma unroll
+                    for (int r = 0; r < 4; r++) p[r][j] = dot4(w[r][j], x[j], p[r][j]);
+            } else if (lane == 0) {
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+            }
             if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
-#pragma unroll
-            for (int j = 0; j < STEPS; j++)
-#pragma unroll
-                for (int r = 0; r < kRows; r++) p[r][j] = dot4(w[r][j], x[j], p[r][j]);
         }
-        float t[kRows];
+        if (nr <= 0) continue;
+        float t[4];
 #pragma unroll
-        for (int r = 0; r < kRows; r++) {
+        for (int r = 0; r < 4; r++) {
             t[r] = 0.f;
 #pragma unroll
             for (int j = 0; j < STEPS; j++) t[r] += p[r][j];
         }
         const float tot = warp_sum4(t[0], t[1], t[2], t[3]);
-        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
-    }
-    return true;
-}
-
-// C = 512 (K an odd multiple of 512, e.g. a tensor-parallel shard): warp w takes 64 columns of each
-// slot, lane l columns 2l, 2l+1
-__device__ __forceinline__ bool consume_512(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
-                                            volatile int *abort_flag, int *err) {
-    constexpr int C = 512;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cw = warp * 64 + lane * 2;
-    for (int ra = r0; ra < r1; ra += kRows) {
-        const int nr = min(kRows, r1 - ra);
-        float p[kRows] = {0.f, 0.f, 0.f, 0.f};
-        for (int c0 = 0; c0 < K; c0 += C) {
-            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err)) return false;
-            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
-            const float2 x = *reinterpret_cast<const float2 *>(xs + c0 + cw);
-            uint32_t w[kRows];
-#pragma unroll
-            for (int r = 0; r < kRows; r++) w[r] = *reinterpret_cast<const uint32_t *>(sa + (size_t)r * C * 2);
-            __syncwarp();
-            if (lane == 0)
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
-            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
-#pragma unroll
-            for (int r = 0; r < kRows; r++) p[r] = fmaf(bf16hi(w[r]), x.y, fmaf(bf16lo(w[r]), x.x, p[r]));
+        if ((lane & 7) == 0 && (lane >> 3) < nr) {
+            float *dst = acc + (ra - r0) + rb + (lane >> 3);
+            if (CB == 1) *dst += tot;  // one warp per row: no other writer
+            else atomicAdd(dst, tot);
         }
-        const float tot = warp_sum4(p[0], p[1], p[2], p[3]);
-        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
     }
     return true;
 }
@@ -268,34 +252,40 @@ __device__ __forceinline__ bool consume(Ring &rg, int N, int K, const float *xs,
         case 4096: ok = consume_c<4096>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
         case 2048: ok = consume_c<2048>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
         case 1024: ok = consume_c<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
-        default: ok = consume_512(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        default: ok = consume_c<512>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
     }
     if (!ok) return false;
     consumers_sync();
     return true;
 }
 
+// This CTA's arrival at a barrier: one release-add on the grid's counter.  The test hook a.stall_cta makes
+// one CTA withhold its arrival at the step's first barrier, so that every wait on it runs out.
+__device__ __forceinline__ void arrive(const StepArgs &a, unsigned idx) {
+    if (idx == 0 && (int)blockIdx.x == a.stall_cta) return;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+}
+
 // every CTA's writes before the barrier are visible to every CTA after it
-__device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned &target, volatile int *abort_flag, int *err,
-                                          unsigned long long *trace = nullptr) {
+__device__ __forceinline__ bool grid_sync(const StepArgs &a, unsigned &target, volatile int *abort_flag) {
     consumers_sync();
     const unsigned idx = target / gridDim.x;
     target += gridDim.x;
-    if (threadIdx.x == 0 && trace && blockIdx.x == 0) trace[2 * idx + 1] = trace_ns();
+    if (threadIdx.x == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 1] = trace_ns();
     if (threadIdx.x == 0) {
         // release: this CTA's writes (ordered before by the named barrier above) are visible to whoever acquires
         // the count; the acquire polls order every later read after the other CTAs' writes
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        arrive(a, idx);
         const uint64_t t0 = now_ns();
-        while (ld_acquire(bar) < target) {
-            if (*abort_flag || ld_acquire(reinterpret_cast<unsigned *>(err)) != 0u) { *abort_flag = 1; break; }
-            if (now_ns() - t0 > kStepWaitNs) {
+        while (ld_acquire(a.bar) < target) {
+            if (*abort_flag || ld_acquire(reinterpret_cast<unsigned *>(a.err)) != 0u) { *abort_flag = 1; break; }
+            if (now_ns() - t0 > a.wait_cycles) {
                 *abort_flag = 1;
-                atomicExch(err, 2);
+                atomicExch(a.err, 2);
                 break;
             }
         }
-        if (trace && blockIdx.x == 0) trace[2 * idx + 2] = trace_ns();
+        if (a.trace && blockIdx.x == 0) a.trace[2 * idx + 2] = trace_ns();
     }
     consumers_sync();
     return !*abort_flag;
@@ -309,53 +299,66 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-__device__ __forceinline__ void red_release_sys(unsigned *p, unsigned v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// What every CTA adds to every rank's exchange buffer before arriving at a cross-rank barrier.
+// What the leader of each rank sends with its arrival at a cross-rank barrier.
 enum { PUB_NONE = 0, PUB_SS = 1 };
 
-// Barrier over every CTA of every tensor-parallel rank, flat: each CTA adds one, with system-scope
-// release semantics, to its rank's arrival counter in every rank's exchange buffer; then every CTA waits until the counters
-// in its own GPU's buffer show all CTAs of all ranks.  Counters grow monotonically across barriers
-// and steps (gen = barriers passed so far), compared with wrap-around arithmetic.  PUB_SS also adds
-// this CTA's q / k sums of squares into every rank's per-layer accumulator.
+// Barrier over every CTA of every tensor-parallel rank, in two levels:
+//   1. every CTA makes its stores into the peers' inboxes visible system-wide (fence.acq_rel.sys) and
+//      arrives at its own grid's counter;
+//   2. lanes 0..tp-1 of CTA 0's first warp wait for the whole grid, then write this rank's generation
+//      number into slot `rank` of every rank's flag array (one NVLink store per peer, no atomics);
+//   3. every CTA waits until the flag array of its own GPU shows the generation for every rank.
+// A rank's flag therefore stands for all of its CTAs.  Generations grow monotonically across barriers and
+// steps (a.gen persists) and are compared with wrap-around arithmetic.  PUB_SS: the q / k sums of squares
+// of the layer (accumulated in this grid by every CTA) travel in the same message, into slot `rank` of the
+// peers' sum arrays, so that every rank adds the tp slots in the same order and gets the same total.
 __device__ __forceinline__ bool cross_sync(const StepArgs &a, unsigned &target, unsigned &gen, int pub, int layer,
                                            float sq, float sk, volatile int *abort_flag) {
     consumers_sync();
     const unsigned idx = target / gridDim.x;
     target += gridDim.x;
     gen += 1u;
-    if (threadIdx.x == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 1] = trace_ns();
-    if (threadIdx.x == 0) {
-        atomicAdd(a.bar, 1u);  // keeps the local barrier counter in step with `target`
-        if (pub == PUB_SS)
-            for (int p = 0; p < a.tp; p++) {
-                float *acc2 = reinterpret_cast<float *>(a.xch[p]) + kXSs + 2 * (layer & 1);  // layer: global count
-                atomicAdd(acc2, sq);
-                atomicAdd(acc2 + 1, sk);
-            }
-        // release at system scope after the CTA barrier orders every thread's stores (the NVLink
-        // stores into the peers' inboxes included) before the arrival
-        for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, 1u);
-        const unsigned want = gen * gridDim.x;
-        const unsigned *mine = a.xch[a.rank] + kXFlags;
-        const uint64_t t0 = now_ns();
-        bool ok = true;
-        for (int p = 0; ok && p < a.tp; p++)
-            while ((int)(ld_acquire_sys(mine + p) - want) < 0)
-                if (*abort_flag || now_ns() - t0 > kStepWaitNs) { ok = false; break; }
-        if (!ok) {
-            *abort_flag = 1;
-            atomicExch(a.err, 4);
+    const int tid = threadIdx.x;
+    if (tid == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 1] = trace_ns();
+    if (tid == 0) {
+        if (pub == PUB_SS) {
+            if (sq != 0.f) atomicAdd(a.ss + 2 * layer, sq);
+            if (sk != 0.f) atomicAdd(a.ss + 2 * layer + 1, sk);
         }
-        if (a.trace && blockIdx.x == 0) a.trace[2 * idx + 2] = trace_ns();
+        fence_sys();  // this CTA's NVLink stores (ordered before by the named barrier) have landed
+        arrive(a, idx);
     }
+    bool ok = true;
+    if (blockIdx.x == 0 && tid < 32) {
+        if (tid == 0) {
+            const uint64_t t0 = now_ns();
+            while (ld_acquire(a.bar) < target)
+                if (*abort_flag || now_ns() - t0 > a.wait_cycles) { ok = false; break; }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (ok && tid < a.tp) {
+            unsigned *peer = a.xch[tid];
+            if (pub == PUB_SS) {
+                float *dst = reinterpret_cast<float *>(peer + kXSs) + 2 * a.rank;
+                dst[0] = __ldcg(a.ss + 2 * layer);
+                dst[1] = __ldcg(a.ss + 2 * layer + 1);
+            }
+            st_release_sys(peer + kXFlags + a.rank, gen);
+        }
+    }
+    if (ok && tid < a.tp) {
+        const unsigned *mine = a.xch[a.rank] + kXFlags + tid;
+        const uint64_t t0 = now_ns();
+        while ((int)(ld_acquire_sys(mine) - gen) < 0)
+            if (*abort_flag || now_ns() - t0 > a.wait_cycles) { ok = false; break; }
+    }
+    if (!ok) {
+        *abort_flag = 1;
+        atomicExch(a.err, 4);
+    }
+    if (tid == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 2] = trace_ns();
     consumers_sync();
     return !*abort_flag;
 }
@@ -570,10 +573,12 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     float scq = 1.f, sck = 1.f;
     if (a.qk_mode == 1) {
         float tq = 0.f, tk = 0.f;
-        if (a.tp > 1) {  // every CTA of every rank added its sums into this rank's accumulator
-            const float *in = reinterpret_cast<const float *>(a.xch[a.rank]) + kXSs + 2 * ((*a.layers_done + layer) & 1);
-            tq = __ldcg(in);
-            tk = __ldcg(in + 1);
+        if (a.tp > 1) {  // every rank's sums, added in rank order (the same total on every rank)
+            const float *in = reinterpret_cast<const float *>(a.xch[a.rank] + kXSs);
+            for (int p = 0; p < a.tp; p++) {
+                tq += __ldcg(in + 2 * p);
+                tk += __ldcg(in + 2 * p + 1);
+            }
         } else {
             tq = __ldcg(a.ss + 2 * layer);
             tk = __ldcg(a.ss + 2 * layer + 1);
@@ -811,7 +816,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
         const uint64_t w0 = now_ns();
         while (ld_acquire(cnt) < (unsigned)ns) {
-            if (now_ns() - w0 > kStepWaitNs) { atomicExch(a.err, 3); break; }
+            if (now_ns() - w0 > a.wait_cycles) { atomicExch(a.err, 3); break; }
         }
     }
     consumers_sync();
@@ -873,7 +878,7 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
 }
 
 template <typename KT, int D, int G, bool TPM>
-__global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kRing], empty_bar[kRing];
     __shared__ int abort_sh;
@@ -897,7 +902,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    Ring rg{full_bar, empty_bar, ring, 0, 0u};
+    Ring rg{full_bar, empty_bar, ring, 0, 0u, a.wait_cycles};
     const int D_ = a.D, Q = a.H * D, KVw = a.Hkv * D, QKV = Q + 2 * KVw, F = a.F;
 
     if (warp == kStepConsumerWarps) {
@@ -925,7 +930,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
                     if (issued >> i & 1u) {
                         const uint32_t addr = su32(&full_bar[i]);
                         const uint64_t t0 = now_ns();
-                        while (!mb_try(addr, (last_ph >> i) & 1u) && now_ns() - t0 < kStepWaitNs) {
+                        while (!mb_try(addr, (last_ph >> i) & 1u) && now_ns() - t0 < a.wait_cycles) {
                         }
                     }
             }
@@ -936,7 +941,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
     // ======================= consumers =======================
     unsigned target = 0;
     unsigned gen = TPM ? *a.gen : 0u;                 // cross-rank barriers passed (monotonic across steps)
-    const unsigned lbase = TPM ? *a.layers_done : 0u;  // layers run by earlier steps (QK-norm sum slots alternate)
     int r0, r1;
     const int token = *a.tokens;
     constexpr bool tpm = TPM;  // tensor parallel: compiled only into the tp > 1 variants
@@ -1007,15 +1011,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
                 }
             }
             if (tpm && a.qk_mode == 1) {
-                // the accumulator slot the next layer uses was last read two layers ago: clear it now
-                // (slots alternate by the global layer count, which continues across steps)
-                if (blockIdx.x == 0 && tid == 0) {
-                    float *nxt = reinterpret_cast<float *>(a.xch[a.rank]) + kXSs + 2 * ((lbase + l + 1) & 1);
-                    nxt[0] = 0.f;
-                    nxt[1] = 0.f;
-                }
-                if (!cross_sync(a, target, gen, PUB_SS, lbase + l, sq, sk, abort_flag)) break;
-            } else if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) {
+                if (!cross_sync(a, target, gen, PUB_SS, l, sq, sk, abort_flag)) break;
+            } else if (!grid_sync(a, target, abort_flag)) {
                 break;
             }
         }
@@ -1026,7 +1023,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             if ((int)blockIdx.x < a.Hkv * ns)
                 attn_item<KT, D, G>(a, Ly, l, blockIdx.x / ns, blockIdx.x % ns, ns, scratch, stage);
         }
-        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        if (!grid_sync(a, target, abort_flag)) break;
         // ---- O projection + residual (summed over ranks through the inboxes) ----
         load_vec(xs, a.attn, Q, nullptr, 0.f, red);
         if (!consume(rg, D_, Q, xs, acc, r0, r1, abort_flag, a.err)) break;
@@ -1037,13 +1034,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             float *t = xcur; xcur = xnext; xnext = t;
         } else {
             for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
-            if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+            if (!grid_sync(a, target, abort_flag)) break;
             load_vec(xs, xcur, D_, Ly.rms_ffn, a.eps, red);
         }
         // ---- gate/up (raw) ----
         if (!consume(rg, 2 * F, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
         for (int r = tid; r < r1 - r0; r += kStepConsumers) a.gu[r0 + r] = acc[r];
-        if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+        if (!grid_sync(a, target, abort_flag)) break;
         // ---- SwiGLU (rows interleaved 16 gate / 16 up) + down + residual ----
         load_swiglu(xs, a.gu, F);
         if (!consume(rg, D_, F, xs, acc, r0, r1, abort_flag, a.err)) break;
@@ -1052,10 +1049,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
         } else {
             for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
-            if (!grid_sync(a.bar, target, abort_flag, a.err, a.trace)) break;
+            if (!grid_sync(a, target, abort_flag)) break;
         }
     }
-    if (*abort_flag) return;
+    if (*abort_flag) {
+        asm volatile("cp.async.wait_all;" ::: "memory");  // staged attention keys still in flight
+        return;
+    }
     // ---- final rmsnorm + lm_head (this rank's vocabulary rows) + argmax ----
     if (tpm) load_resid(a, xs, xcur, box_d, xnext, a.norm_final, red);
     else load_vec(xs, xcur, D_, a.norm_final, a.eps, red);
@@ -1094,7 +1094,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
     if (lane == 0) {
         const uint64_t t0 = now_ns();
         while (ld_acquire(a.bar) < target)
-            if (now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+            if (now_ns() - t0 > a.wait_cycles) { ok = false; break; }
     }
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     __threadfence();
@@ -1112,25 +1112,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
     if (tpm) {
-        // one more flat barrier in which only CTA 0 of each rank takes part: its counter slot grows
-        // by gridDim.x so that the counters stay multiples of the grid
+        // every rank's winner: lane p sends this rank's (value, index) into slot `rank` of rank p's array and
+        // then its generation flag; then lanes 0..tp-1 wait for every rank's flag
         gen += 1u;
-        if (lane == 0 && ok) {
-            for (int p = 0; p < a.tp; p++) {
-                unsigned *in = a.xch[p] + kXAm + 2 * a.rank;
-                in[0] = __float_as_uint(bv);
-                in[1] = (unsigned)bi;
-            }
-            __threadfence_system();
-            for (int p = 0; p < a.tp; p++) red_release_sys(a.xch[p] + kXFlags + a.rank, gridDim.x);
-            const unsigned want = gen * gridDim.x;
-            const unsigned *mine = a.xch[a.rank] + kXFlags;
-            const uint64_t t0 = now_ns();
-            for (int p = 0; ok && p < a.tp; p++)
-                while ((int)(ld_acquire_sys(mine + p) - want) < 0)
-                    if (now_ns() - t0 > kStepWaitNs) { ok = false; break; }
+        if (ok && lane < a.tp) {
+            unsigned *in = a.xch[lane] + kXAm + 2 * a.rank;
+            in[0] = __float_as_uint(bv);
+            in[1] = (unsigned)bi;
+            st_release_sys(a.xch[lane] + kXFlags + a.rank, gen);
         }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (ok && lane < a.tp) {
+            const unsigned *mine = a.xch[a.rank] + kXFlags + lane;
+            const uint64_t t0 = now_ns();
+            while ((int)(ld_acquire_sys(mine) - gen) < 0)
+                if (now_ns() - t0 > a.wait_cycles) { ok = false; break; }
+        }
+        ok = __all_sync(0xffffffffu, ok);
         bv = -FLT_MAX;
         bi = INT_MAX;
         if (lane < a.tp) {
@@ -1156,20 +1153,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepArgs a)
             *a.tokens = bi;
             *a.positions += 1;
         }
-        if (TPM) {
-            *a.gen = gen;
-            *a.layers_done = lbase + a.layers;
-        }
+        if (TPM) *a.gen = gen;
     }
 }
 
 template <typename KT, int D, bool TPM>
 const void *step_fn_g(int G) {
     switch (G) {
-        case 1: return (const void *)step_kernel<KT, D, 1, TPM>;
-        case 2: return (const void *)step_kernel<KT, D, 2, TPM>;
-        case 4: return (const void *)step_kernel<KT, D, 4, TPM>;
-        case 8: return (const void *)step_kernel<KT, D, 8, TPM>;
+        case 1: return (const void *)qw_step_kernel<KT, D, 1, TPM>;
+        case 2: return (const void *)qw_step_kernel<KT, D, 2, TPM>;
+        case 4: return (const void *)qw_step_kernel<KT, D, 4, TPM>;
+        case 8: return (const void *)qw_step_kernel<KT, D, 8, TPM>;
     }
     return nullptr;
 }

@@ -34,8 +34,8 @@ class QwConfig(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "dim", "hidden_dim", "layers", "heads", "kv_heads", "head_dim", "vocab", "seq_len", "shared_weights",
         "qk_norm", "has_qkv_bias", "weight_dtype", "kv_dtype", "max_batch", "max_tokens", "page_size", "num_pages",
-        "decode_kernels")] + \
-        [("reserved", C.c_int32 * 4), ("rope_theta", C.c_double), ("eps", C.c_double)]
+        "decode_kernels", "wait_limit_us", "test_stall_cta")] + \
+        [("reserved", C.c_int32 * 2), ("rope_theta", C.c_double), ("eps", C.c_double)]
 
 
 class QwenError(RuntimeError):
@@ -110,13 +110,14 @@ def _fp(a):
 def make_config(dim, hidden_dim, layers, heads, kv_heads, head_dim, vocab, seq_len, shared_weights=False,
                 qk_norm=QKNORM_VECTOR, has_qkv_bias=False, weight_dtype=DTYPE_BF16, kv_dtype=DTYPE_BF16,
                 max_batch=1, max_tokens=0, page_size=64, num_pages=0, rope_theta=1e6, eps=1e-6,
-                decode_kernels=0) -> QwConfig:
+                decode_kernels=0, wait_limit_us=0, test_stall_cta=0) -> QwConfig:
     c = QwConfig()
     c.dim, c.hidden_dim, c.layers, c.heads, c.kv_heads, c.head_dim = dim, hidden_dim, layers, heads, kv_heads, head_dim
     c.vocab, c.seq_len, c.shared_weights, c.qk_norm, c.has_qkv_bias = vocab, seq_len, int(shared_weights), qk_norm, int(has_qkv_bias)
     c.weight_dtype, c.kv_dtype, c.max_batch, c.max_tokens = weight_dtype, kv_dtype, max_batch, max_tokens or max_batch
     c.page_size, c.num_pages, c.rope_theta, c.eps = page_size, num_pages, rope_theta, eps
     c.decode_kernels = decode_kernels
+    c.wait_limit_us, c.test_stall_cta = wait_limit_us, test_stall_cta
     return c
 
 

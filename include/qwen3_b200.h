@@ -80,7 +80,13 @@ typedef struct qw_config {
                                tp 1, one kernel per operation + NCCL under tensor parallelism), 1 = one
                                kernel per operation, 2 = the persistent kernel at any tp (cross-GPU
                                exchange over NVLink peer memory) */
-    int32_t reserved[4];
+    int32_t wait_limit_us;  /* bound of every device-side wait (grid and cross-GPU barriers, copies in flight,
+                               split merges) in microseconds; 0 = 2 s.  A wait that runs out stops the kernel,
+                               which records the site; qw_synchronize then returns QW_ERR_TIMEOUT */
+    int32_t test_stall_cta; /* test hook, 0 = off: CTA (test_stall_cta - 1) of the persistent decode step
+                               withholds its arrival at the step's first barrier, so that the other CTAs' bounded
+                               waits run out (exercises the QW_ERR_TIMEOUT path without a GPU fault) */
+    int32_t reserved[2];
     double rope_theta;      /* 1e6 for Qwen3 */
     double eps;             /* rmsnorm epsilon, 1e-6 for Qwen3 */
 } qw_config;

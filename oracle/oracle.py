@@ -62,6 +62,7 @@ def lib(precision: str = "f64") -> C.CDLL:
             "oref_rmsnorm": (None, [D, D, I, C.c_double, D]),
             "oref_argmax": (I, [F, I]),
             "oref_num_threads": (I, []),
+            "oref_set_threads": (None, [I]),
             "oref_bench_slice": (I, [P, I, I, I, I]),
         }
         for name, (res, args) in sig.items():
@@ -144,8 +145,14 @@ def synth_value(seed: int, tensor_id: int, idx: int, scale: float) -> float:
     return float(lib("f64").oref_synth_value(seed, tensor_id, idx, scale))
 
 
-def num_threads() -> int:
-    return int(lib("f64").oref_num_threads())
+def num_threads(precision: str = "f64") -> int:
+    return int(lib(precision).oref_num_threads())
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of both oracle builds (overrides OMP_NUM_THREADS, which torchrun sets to 1)."""
+    for p in ("f64", "f32"):
+        lib(p).oref_set_threads(int(n))
 
 
 # ------------------------------------------------------------------ full model

@@ -472,6 +472,15 @@ int API(oref_generate)(void *mp, const int *prompt, int prompt_len, int steps, i
     return 0;
 }
 
+/* host threads for the timed CPU baseline (a torchrun launch sets OMP_NUM_THREADS=1 in the environment) */
+void API(oref_set_threads)(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int API(oref_num_threads)(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();
