@@ -206,6 +206,18 @@ def run_batched(args, rank, world, local, nid, peaks):
                "timing": "qw_prefill through the host API (tokens from host memory), CUDA events, best of "
                          f"{args.prefill_reps}" if world == 1 else "max over ranks"}
 
+    # per-kernel split of one prefill (CUDA events around every launch)
+    pk_ms, pk_kind = m.profile_prefill(prompts[:NSEQ])
+    split = {}
+    for x, kk in zip(pk_ms, pk_kind):
+        split[native.KERNEL_NAMES[int(kk)]] = split.get(native.KERNEL_NAMES[int(kk)], 0.0) + float(x)
+    prefill["kernel_ms"] = split
+    if split.get("attn"):
+        att_tf = att / world / (split["attn"] * 1e-3) / 1e12
+        prefill["attention"] = {"kernel": "qw_flash_prefill_tc_kernel (tcgen05, TMEM, TMA)"
+                                if os.environ.get("QW_TC_ATTN", "1") != "0" else "qw_flash_prefill_kernel (mma.sync)", "ms": split["attn"],
+                                "flops": att / world, "tflops": att_tf, "frac": att_tf / peak_tf,
+                                "flops_counted": "causal: 2 * 2 * L^2 / 2 * head_dim per head, layer and sequence"}
     # ---- batch-B decode at context L: prefill the remaining slots, capture, replay ----
     for c0 in range(NSEQ, B, NSEQ):
         m.prefill(prompts[c0:c0 + NSEQ], slots=np.arange(c0, min(B, c0 + NSEQ), dtype=np.int32), want_logits=False)

@@ -24,7 +24,7 @@
 // and the first S weight tiles overlap the end of the previous kernel in the stream; the
 // activation tiles and the epilogue wait for it (griddepcontrol.wait).
 //
-// Every mbarrier wait is bounded (kTcWaitNs); on expiry the CTA records TC_DEVERR_TIMEOUT,
+// Every mbarrier wait is bounded (kTcuWaitCycles); on expiry the CTA records TC_DEVERR_TIMEOUT,
 // lets its issued copies and MMAs land, frees its TMEM and returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -32,6 +32,7 @@
 
 #include "qw_internal.cuh"
 #include "qw_tc.h"
+#include "qw_tc_util.cuh"
 
 namespace qw {
 
@@ -40,109 +41,14 @@ namespace {
 constexpr int kTcThreads = 192;
 constexpr int kBM = 128, kBK = 64;
 constexpr int kGroupT = 8;
-constexpr unsigned long long kTcWaitNs = 4000ull * 1000ull * 1000ull;  // cycles: ~2 s at 2 GHz
 constexpr int kTcSmemBudget = 196 * 1024;
 
+__host__ __device__ constexpr uint32_t tc_idesc(int bn) { return tc_idesc_f16(kBM, bn); }
 __host__ __device__ constexpr int tc_stage_bytes(int bn) { return (kBM + bn) * kBK * 2; }
 __host__ __device__ constexpr int tc_stages(int bn) {
     return kTcSmemBudget / tc_stage_bytes(bn) > 8 ? 8 : kTcSmemBudget / tc_stage_bytes(bn);
 }
 __host__ __device__ constexpr int tc_smem_bytes(int bn) { return tc_stages(bn) * tc_stage_bytes(bn) + 1024 + 4096; }
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-// cycle counter of this SM: cheap to read in a spin loop (the bounds below are in cycles)
-__device__ __forceinline__ uint64_t gtime_ns() { return (uint64_t)clock64(); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-
-// Bounded wait: false when the CTA is aborting or the limit expired (which starts the abort).
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, int *err) {
-    const uint32_t addr = smem_u32(b);
-    if (mbar_try(addr, parity)) return true;
-    const uint64_t t0 = gtime_ns();
-    for (;;) {
-        if (mbar_try(addr, parity)) return true;
-        if (*abort_flag) return false;
-        if (gtime_ns() - t0 > kTcWaitNs) {
-            *abort_flag = 1;
-            if (err) atomicExch(err, TC_DEVERR_TIMEOUT);
-            return false;
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major tile, rows of 128 bytes with the 128-byte swizzle,
-// 8-row core groups 1024 bytes apart (stride byte offset), descriptor version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)1 << 16;            // leading byte offset (unused by swizzled K-major layouts)
-    d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset
-    d |= (uint64_t)1 << 46;            // version
-    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
-    return d;
-}
-
-// Instruction descriptor of kind::f16: bf16 A and B (both K-major), fp32 D, M = 128, N = bn.
-__host__ __device__ constexpr uint32_t tc_idesc(int bn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 struct TileCoord {
     int f0, t0, kb0, kb1, ks;
@@ -254,7 +160,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (issued >> i & 1u) {
                         const uint32_t addr = smem_u32(&full_bar[i]);
                         const uint64_t t0 = gtime_ns();
-                        while (!mbar_try(addr, (last_ph >> i) & 1u) && gtime_ns() - t0 < kTcWaitNs) {
+                        while (!mbar_try(addr, (last_ph >> i) & 1u) && gtime_ns() - t0 < kTcuWaitCycles) {
                         }
                     }
             }
@@ -289,7 +195,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_commit(&done_bar);
             const uint32_t addr = smem_u32(&done_bar);
             const uint64_t t0 = gtime_ns();
-            while (!mbar_try(addr, 0) && gtime_ns() - t0 < kTcWaitNs) {
+            while (!mbar_try(addr, 0) && gtime_ns() - t0 < kTcuWaitCycles) {
             }
         }
     } else {
@@ -380,36 +286,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
 // bf16 (rows, cols) row-major, box of box_rows x 64 columns, 128-byte swizzle, zero fill
 cudaError_t make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return cudaErrorNotSupported;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols % 8)) return cudaErrorMisalignedAddress;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+    return tma_map_bf16_sw128(m, base, rows, cols, cols, box_rows);
 }
 
 template <int BN, int EPI>
@@ -433,6 +312,38 @@ cudaError_t launch_epi(const CUtensorMap &mw, const CUtensorMap &mx, const TcArg
 }
 
 }  // namespace
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+cudaError_t tma_map_bf16_sw128(CUtensorMap *m, const void *base, long long rows, int cols, int ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld % 8) || cols > ld || box_rows < 1 || box_rows > 256)
+        return cudaErrorMisalignedAddress;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
 
 cudaError_t tc_prepare() {
     const void *fns[] = {(const void *)qw_tc_gemm_kernel<64, TC_STORE>,  (const void *)qw_tc_gemm_kernel<128, TC_STORE>,

@@ -83,6 +83,8 @@ struct FlashArgs {
     float scale;
     __nv_bfloat16 *out;  // (nseq * L, ld_out)
     int ld_out;
+    int num_pages;  // pages of the KV pool (the tensor-core kernel's TMA descriptor of the cache)
+    int *err;       // device error word (bounded waits)
 };
 
 struct FlashDecodeArgs {
@@ -135,6 +137,9 @@ unsigned long long java_random_state(long long seed);
 cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st);
 cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st);
 cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st);
+// head_dim 128 on tcgen05 (qw_attn_tc.cu); flash_prefill_tc_prepare opts it in to its shared memory
+cudaError_t flash_prefill_tc_launch(const FlashArgs &a, int nseq, cudaStream_t st);
+cudaError_t flash_prefill_tc_prepare();
 cudaError_t rows_argmax_launch(const RowsArgmaxArgs &a, int rows, cudaStream_t st);
 cudaError_t flash_decode_launch(const FlashDecodeArgs &a, int B, cudaStream_t st);
 cudaError_t prefill_kernels_prepare();  // opt the row kernels in to their shared memory (once, before capture)
@@ -184,6 +189,7 @@ struct StepArgs {
     unsigned long long *trace;       // optional: CTA 0's globaltimer before / after every grid barrier
     int evict_first;                 // weight stream marked L2 evict-first (keeps code, KV and activations resident)
     unsigned long long wait_cycles;  // bound of every wait in SM clock cycles; on expiry the kernel reports and returns
+    int row_copies;                  // ring: one bulk copy per weight row (else one per slot when rows are contiguous)
     int stall_cta;                   // test hook (-1 = off): this CTA withholds its arrival at the step's first barrier
 };
 

@@ -81,6 +81,7 @@ struct qw_model {
     int hist_ld = 0;
     int *h_pin_i = nullptr;  // pinned staging: tokens | positions | slots | argmax
     PrefillBuffers pf{};
+    bool tc_attn = false;  // prefill attention on tcgen05 (head_dim 128)
     // persistent batch-1 step kernel
     bool use_step = false;
     StepArgs step{};
@@ -574,7 +575,9 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             fa.max_pages = m->max_pages; fa.page_size = m->page_size; fa.log2_page = m->log2_page;
             fa.seq_slots = seq_slots; fa.p0 = p0; fa.L = L; fa.H = m->Hl; fa.Hkv = m->Hkvl; fa.d = d;
             fa.scale = (float)(1.0 / sqrt((double)d)); fa.out = pf.act; fa.ld_out = m->Ql;
-            LKK(QW_KERNEL_ATTN, flash_prefill_launch(fa, nseq, m->st));
+            fa.num_pages = m->num_pages; fa.err = pf.d_err;
+            if (d == 128 && m->tc_attn) LKK(QW_KERNEL_ATTN, flash_prefill_tc_launch(fa, nseq, m->st));
+            else LKK(QW_KERNEL_ATTN, flash_prefill_launch(fa, nseq, m->st));
         } else {
             FlashDecodeArgs fd{};
             fd.q = pf.q; fd.ld_q = m->Ql; fd.kcache = kc; fd.vcache = vc; fd.page_table = m->d_page_table;
@@ -972,6 +975,12 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
     if (m->pf.tc) {
         CK(tc_prepare());
         CK(prefill_kernels_prepare());
+        if (c.head_dim == 128) {
+            // causal prefill attention on tcgen05 (QW_TC_ATTN=0: the mma.sync kernel, for comparison)
+            const char *ev = getenv("QW_TC_ATTN");
+            m->tc_attn = !ev || atoi(ev) != 0;
+            if (m->tc_attn) CK(flash_prefill_tc_prepare());
+        }
         AL(m->gu_split, (size_t)B * 2 * m->Fl);
     }
     // the persistent step kernel: automatic at tp 1; under tensor parallelism only when asked for
@@ -1010,6 +1019,8 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 {
                     const char *ev = getenv("QW_STEP_EVICT");
                     sa.evict_first = ev ? atoi(ev) : 1;
+                    const char *rc = getenv("QW_STEP_ROWCOPY");
+                    sa.row_copies = rc ? atoi(rc) : 0;
                 }
                 {
                     int khz = 0;
@@ -1312,6 +1323,33 @@ qw_status qw_generate(qw_model *m, const int32_t *prompts, int32_t batch, int32_
     if (e != cudaSuccess) return fail(m, QW_ERR_CUDA, "generate: %s", cudaGetErrorString(e));
     for (int b = 0; b < batch; b++)
         for (int i = prompt_len; i < steps; i++) tokens_out[(size_t)b * steps + i] = h[(size_t)b * (steps + 1) + i];
+    return QW_OK;
+}
+
+qw_status qw_profile_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, int32_t batch, int32_t seq_len,
+                             float *ms_out, int32_t *kinds_out, int32_t cap, int32_t *n_out) {
+    if (!m || !tokens || !ms_out || !kinds_out || !n_out || cap < 1)
+        return m ? fail(m, QW_ERR_ARG, "null argument") : QW_ERR_ARG;
+    if (!m->pf.tc) return fail(m, QW_ERR_UNSUPPORTED, "prefill profiling needs the tensor-core path (bf16)");
+    if (batch < 1 || batch > m->B || seq_len < 1) return fail(m, QW_ERR_SHAPE, "batch %d / seq_len %d", batch, seq_len);
+    CK(cudaSetDevice(m->dev));
+    while ((int)m->prof_ev.size() < 2 * cap) {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        m->prof_ev.push_back(e);
+    }
+    m->prof_kinds.assign(cap, 0);
+    m->prof_n = 0;
+    m->prof_on = true;
+    qw_status s = tc_prefill(m, tokens, slots, batch, seq_len, nullptr, nullptr);
+    m->prof_on = false;
+    if (s) return s;
+    CK(cudaStreamSynchronize(m->st));
+    for (int i = 0; i < m->prof_n; i++) {
+        CK(cudaEventElapsedTime(&ms_out[i], m->prof_ev[2 * i], m->prof_ev[2 * i + 1]));
+        kinds_out[i] = m->prof_kinds[i];
+    }
+    *n_out = m->prof_n;
     return QW_OK;
 }
 

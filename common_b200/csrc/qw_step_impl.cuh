@@ -111,6 +111,7 @@ struct Ring {
     int slot;
     uint32_t ph;
     unsigned long long lim;  // wait bound (cycles)
+    int row_copies;          // one copy per row even when a slot's rows are contiguous
 };
 
 // Column chunk of one ring slot.  A slot holds the same C columns of R = 16384 / C consecutive rows
@@ -136,8 +137,9 @@ __device__ __forceinline__ bool produce(Ring &rg, const __nv_bfloat16 *W, int N,
             const uint32_t fb = su32(&rg.full[rg.slot]);
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb), "r"((uint32_t)(nr * C * 2))
                          : "memory");
-            const int ncopy = C == K ? 1 : nr;
-            const uint32_t bytes = (uint32_t)((C == K ? nr : 1) * C * 2);
+            const bool whole = C == K && !rg.row_copies;
+            const int ncopy = whole ? 1 : nr;
+            const uint32_t bytes = (uint32_t)((whole ? nr : 1) * C * 2);
             for (int j = 0; j < ncopy; j++)
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
@@ -199,7 +201,7 @@ __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, floa
             for (int j = 0; j < STEPS; j++) p[r][j] = 0.f;
         for (int c0 = 0; c0 < K; c0 += C) {
             if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err, rg.lim)) return false;
-            if (nr > 0) {
+            if (CB == kStepConsumerWarps || nr > 0) {  // one row block per slot: every warp has rows
                 const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + ((size_t)rb * C + cw) * 2;
                 const float *xp = xs + c0 + cw;
                 float4 x[STEPS];
@@ -223,7 +225,7 @@ __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, floa
             }
             if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
         }
-        if (nr <= 0) continue;
+        if (CB != kStepConsumerWarps && nr <= 0) continue;
         float t[4];
 #pragma unroll
         for (int r = 0; r < 4; r++) {
@@ -241,6 +243,14 @@ __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, floa
     return true;
 }
 
+// The narrow slot shapes (tensor-parallel shards, small models) out of line: the 8B geometry at tp 1 runs
+// only C = 4096, and keeping the others out of the kernel body keeps its hot code compact.
+template <int C>
+__device__ __noinline__ bool consume_narrow(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+                                            volatile int *abort_flag, int *err) {
+    return consume_c<C>(rg, K, xs, acc, r0, r1, abort_flag, err);
+}
+
 __device__ __forceinline__ bool consume(Ring &rg, int N, int K, const float *xs, float *acc, int &r0, int &r1,
                                         volatile int *abort_flag, int *err) {
     split_rows(N, blockIdx.x, gridDim.x, r0, r1);
@@ -250,9 +260,9 @@ __device__ __forceinline__ bool consume(Ring &rg, int N, int K, const float *xs,
     bool ok;
     switch (chunk_cols(K)) {
         case 4096: ok = consume_c<4096>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
-        case 2048: ok = consume_c<2048>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
-        case 1024: ok = consume_c<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
-        default: ok = consume_c<512>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 2048: ok = consume_narrow<2048>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 1024: ok = consume_narrow<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        default: ok = consume_narrow<512>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
     }
     if (!ok) return false;
     consumers_sync();
@@ -902,7 +912,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    Ring rg{full_bar, empty_bar, ring, 0, 0u, a.wait_cycles};
+    Ring rg{full_bar, empty_bar, ring, 0, 0u, a.wait_cycles, a.row_copies};
     const int D_ = a.D, Q = a.H * D, KVw = a.Hkv * D, QKV = Q + 2 * KVw, F = a.F;
 
     if (warp == kStepConsumerWarps) {

@@ -5,6 +5,7 @@
 // features per tile) and the tokens are its N side (64, 128 or 256 per tile), so the same
 // kernel serves prefill (T in the thousands) and batched decode (T = batch).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -36,6 +37,10 @@ struct TcArgs {
 // Build the TMA descriptors and launch.  bn = 0 picks the token tile from T.
 cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int epi, int bn, int num_sms,
                            cudaStream_t st);
+
+// TMA descriptor of a bf16 (rows, cols) row-major matrix with row stride ld elements: boxes of box_rows x 64
+// columns (128 bytes), 128-byte swizzle, zero fill out of bounds.  base 16-byte aligned, ld a multiple of 8.
+cudaError_t tma_map_bf16_sw128(CUtensorMap *m, const void *base, long long rows, int cols, int ld, int box_rows);
 
 // Opt every GEMM variant in to its shared memory (once per device, outside of stream capture).
 cudaError_t tc_prepare();

@@ -26,7 +26,7 @@ EXPORTS = ("qw_abi_version", "qw_build_info", "qw_get_unique_id", "qw_create", "
            "qw_finalize_weights", "qw_reset", "qw_reserve", "qw_decode_step", "qw_forward_hidden", "qw_prefill",
            "qw_generate", "qw_decode_step_device", "qw_capture_decode", "qw_replay_decode", "qw_synchronize",
            "qw_stream", "qw_last_launch_count", "qw_last_error", "qw_destroy", "qw_profile_decode",
-           "qw_set_device_inputs", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static", "qw_op_linear", "qw_set_sampling", "qw_decode_sample", "qw_op_sample")
+           "qw_set_device_inputs", "qw_profile_prefill", "qw_op_lm_head_argmax", "qw_op_lm_head_argmax_static", "qw_op_linear", "qw_set_sampling", "qw_decode_sample", "qw_op_sample")
 KERNEL_NAMES = {0: "other", 1: "qkv", 2: "attn", 3: "o_proj", 4: "gate_up", 5: "down", 6: "lm_head", 7: "step"}
 
 
@@ -78,6 +78,7 @@ def load() -> C.CDLL:
         "qw_capture_decode": (I32, [P, P, P, P, I32, P, P]),
         "qw_replay_decode": (I32, [P, I32]),
         "qw_synchronize": (I32, [P]),
+        "qw_profile_prefill": (I32, [P, PI, PI, I32, I32, PF, PI, I32, PI]),
         "qw_stream": (P, [P]),
         "qw_last_launch_count": (I32, [P]),
         "qw_last_error": (C.c_char_p, [P]),
@@ -92,6 +93,8 @@ def load() -> C.CDLL:
         "qw_op_lm_head_argmax_static": (I32, [P, I32, I32, I32, P, P, C.c_double, I32, P, P, P]),
     }
     for name, (res, args) in sig.items():
+        if os.environ.get("QW_LIB") and not hasattr(L, name):
+            continue  # another build (QW_LIB) may predate an entry point
         fn = getattr(L, name)
         fn.restype = res
         fn.argtypes = args
@@ -307,6 +310,17 @@ class NativeModel:
         kinds = np.zeros(cap, np.int32)
         n = C.c_int32(0)
         self._check(self.L.qw_profile_decode(self.h, batch, _fp(ms), _ip(kinds), cap, C.byref(n)))
+        return ms[: n.value].copy(), kinds[: n.value].copy()
+
+    def profile_prefill(self, tokens, slots=None, cap: int = 8192):
+        """Per-kernel CUDA-event durations (ms) and classes of one prefill of (batch, seq_len) tokens."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        s = None if slots is None else np.ascontiguousarray(slots, np.int32)
+        ms = np.zeros(cap, np.float32)
+        kinds = np.zeros(cap, np.int32)
+        n = C.c_int32(0)
+        self._check(self.L.qw_profile_prefill(self.h, _ip(t), _ip(s), t.shape[0], t.shape[1], _fp(ms), _ip(kinds), cap,
+                                              C.byref(n)))
         return ms[: n.value].copy(), kinds[: n.value].copy()
 
     @property

@@ -227,6 +227,13 @@ qw_status qw_set_device_inputs(qw_model *m, const int32_t *tokens, const int32_t
 qw_status qw_profile_decode(qw_model *m, int32_t batch, float *ms_out, int32_t *kinds_out, int32_t cap,
                             int32_t *n_out);
 
+/* qw_prefill of (batch, seq_len) host tokens with CUDA events around every kernel launch (tensor-core
+ * path only); writes up to `cap` launch durations (ms) and their QW_KERNEL_* classes and the launch count
+ * to *n_out.  Stands in for nothing in the reference (a measurement aid; the reference feeds prompts one
+ * token per forward, AutoregressiveModel.java:296-299). */
+qw_status qw_profile_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, int32_t batch, int32_t seq_len,
+                             float *ms_out, int32_t *kinds_out, int32_t cap, int32_t *n_out);
+
 /* Wait for all work on the model's stream; QW_ERR_TIMEOUT if a bounded device-side wait gave up
  * since the model was created (a peer rank that never arrived, for instance). */
 qw_status qw_synchronize(qw_model *m);

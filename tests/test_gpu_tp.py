@@ -57,18 +57,14 @@ def test_tp2_matches_oracle():
             want = ob.forward_token(int(seqs[b, p]), p)
         assert rel_l2(out["batch6"][b], want) < 2e-2
         ob.close()
-    # greedy tokens of the tensor-parallel step kernel: the oracle's argmax at every step, or a near-tie
+    # greedy tokens of the tensor-parallel step kernel: exactly the oracle's (fixture tp_parity.npz, whose
+    # seed leaves every greedy choice a margin far above the bf16 error)
     assert out["step_launches"] == 1
     got = out["greedy"]
     np.testing.assert_array_equal(res[1]["greedy"], got)
-    from tests.tp_worker import step_cfg
-    c2, sd2 = step_cfg()
-    ob = oracle_model(c2, sd2, bf16_weights=True)
-    for p in range(len(got) - 1):
-        lg = ob.forward_token(int(got[p]), p)
-        if p >= 7 and int(np.argmax(lg)) != int(got[p + 1]):
-            assert lg.max() - lg[int(got[p + 1])] < 2e-2 * lg.std(), p
-    ob.close()
+    from tests.tp_worker import parity_fixture
+    _, fx = parity_fixture()
+    np.testing.assert_array_equal(got, fx["bf16_tokens"][:len(got)])
     assert out["graph"] == [int(t) for t in got[9:]]
     # both ranks return the full (gathered) logits
     np.testing.assert_allclose(res[1]["fp32"][5], out["fp32"][5], rtol=1e-5, atol=1e-6)

@@ -3,11 +3,13 @@ own NCCL unique id: an id bootstraps exactly one communicator."""
 import numpy as np
 
 
-def step_cfg():
-    """A geometry the persistent step kernel runs at tp 2: dim, local q width and intermediate multiples of 512."""
-    from tests.helpers import cfg_dict, state_dict
-    c = cfg_dict(dim=1024, hidden_dim=2048, layers=2, heads=8, kv_heads=2, head_dim=128, vocab=2000, seq_len=64)
-    return c, state_dict(c, seed=54, std=0.05, norm_noise=0.1)
+def parity_fixture():
+    """The model and the oracle's answers of tests/golden/tp_parity.npz (made by make_tp_parity.py): the
+    library's synthetic weights at a geometry whose tp-2 shard runs the persistent step kernel."""
+    import os
+    from tests.golden.make_tp_parity import GEOM
+    fx = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tp_parity.npz"))
+    return GEOM, fx
 
 
 def run_rank(rank, world, nids, c, q):
@@ -32,15 +34,21 @@ def run_rank(rank, world, nids, c, q):
         out["batch6"] = last
         m.close()
         # bf16 batch-1 greedy generation: the persistent step kernel with the cross-rank exchange over NVLink
-        c, sd = step_cfg()
-        m = native_model_tp(c, sd, "bf16", rank, world, nids[2], max_batch=1, max_tokens=8, decode_kernels=2)
-        out["greedy"] = m.generate(np.array([3, 1, 4, 1, 5, 9, 2, 6], np.int32), 8 + 24)[0]
+        g, fx = parity_fixture()
+        cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
+                                 g["vocab"], g["seq_len"], False, native.QKNORM_VECTOR, False, native.DTYPE_BF16,
+                                 native.DTYPE_BF16, 1, 8, decode_kernels=2)
+        m = native.NativeModel(cfg, rank, rank, world, nids[2])
+        m.init_synthetic(int(fx["seed"]), float(fx["std"]))
+        m.finalize()
+        prompt = fx["prompt"].astype(np.int32)
+        out["greedy"] = m.generate(prompt, 8 + 24)[0]
         out["step_launches"] = m.last_launch_count  # 1: the persistent step kernel ran
         # the same greedy steps replayed from a captured CUDA graph (token/position advance on the device)
         import torch
         torch.cuda.set_device(rank)
         m.reset()
-        m.prefill(np.array([[3, 1, 4, 1, 5, 9, 2, 6]], np.int32), want_logits=False)
+        m.prefill(prompt[None], want_logits=False)
         m.reserve(0, 40)
         dt = torch.tensor([int(out["greedy"][8])], dtype=torch.int32, device="cuda")
         dp = torch.tensor([8], dtype=torch.int32, device="cuda")
