@@ -179,10 +179,8 @@ struct StepArgs {
     // tensor parallelism (tp = 1: none)
     int tp, rank, v0;          // ranks, this rank, first vocabulary row of this rank's lm_head shard
     int q_total, kv_total;     // global q / k widths (whole-vector QK-norm denominators)
-    float *x2;                 // second residual-stream buffer (tp > 1)
     unsigned *const *xch;      // device array [tp]: every rank's exchange buffer (peer pointers)
     unsigned *gen;             // cross-rank barriers passed, persistent across steps
-    unsigned *layers_done;     // layers run by earlier steps, persistent
     int max_k, max_rows, xs_floats;  // shared-memory layout
     int stage_off;                   // floats: staged attention keys within the activation region
     int kv_bf16;

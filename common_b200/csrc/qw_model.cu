@@ -832,7 +832,7 @@ qw_status qw_get_unique_id(void *out128) {
 // handle through an NCCL all-gather and opens the others' (peer access over NVLink).
 static qw_status setup_exchange(qw_model *m) {
     const int tp = m->tp;
-    const size_t words = 128 + (size_t)2 * tp * m->D;
+    const size_t words = 128 + (size_t)4 * tp * m->D;  // flags, sums, argmax, two [tp][D] inboxes of 8-byte words
     CK(cudaMalloc((void **)&m->xch, words * sizeof(unsigned)));
     CK(cudaMemset(m->xch, 0, words * sizeof(unsigned)));
     cudaIpcMemHandle_t h;
@@ -1031,11 +1031,9 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
                 }
                 sa.tp = tp_size; sa.rank = tp_rank; sa.v0 = m->v0;
                 sa.q_total = c.heads * c.head_dim; sa.kv_total = c.kv_heads * c.head_dim;
-                sa.x2 = m->xb;
                 AL(m->d_persist, 2);
                 CK(cudaMemset(m->d_persist, 0, 2 * sizeof(unsigned)));
                 sa.gen = m->d_persist;
-                sa.layers_done = m->d_persist + 1;
                 if (tp_size > 1) {
                     qw_status st = setup_exchange(m);
                     if (st) return st;

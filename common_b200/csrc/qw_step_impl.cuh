@@ -44,9 +44,9 @@ constexpr int kPiece = 32768;  // bytes per ring slot (16384 bf16 weights: R row
 constexpr int kRing = 5;
 // layout of a rank's exchange buffer (32-bit words): flags, QK-norm sums, argmax, row partials
 constexpr int kXFlags = 0;   // [tp] generation flags, written by each peer
-constexpr int kXSs = 64;     // [tp][2] q / k sums of squares of the current layer, one slot per rank
+constexpr int kXSs = 64;     // [tp][2] 8-byte words: q / k sums of squares of the current layer, one slot per rank
 constexpr int kXAm = 96;     // [tp][2] (value, index) of each rank's vocabulary shard
-constexpr int kXRows = 128;  // [2][tp][D]: O partials, then down partials
+constexpr int kXRows = 128;  // [2][tp][D] 8-byte words: O partials, then down partials
 constexpr int kStepTPW = 4;  // attention: keys per warp per tile (small: this code runs once per layer, cold in the instruction cache)
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -243,10 +243,137 @@ __device__ __forceinline__ bool consume_c(Ring &rg, int K, const float *xs, floa
     return true;
 }
 
-// The narrow slot shapes (tensor-parallel shards, small models) out of line: the 8B geometry at tp 1 runs
-// only C = 4096, and keeping the others out of the kernel body keeps its hot code compact.
+// ---- the 4-row ring of the tp = 1 kernel: every slot holds 4 rows of up to 4096 columns ----
+// (the tensor-parallel kernel uses the rows x columns slots above, whose narrow shards need them)
+__device__ __forceinline__ bool produce_r4(Ring &rg, const __nv_bfloat16 *W, int N, int K, volatile int *abort_flag,
+                                        int *err, uint32_t &issued, uint32_t &last_ph, uint64_t policy) {
+    int r0, r1;
+    split_rows(N, blockIdx.x, gridDim.x, r0, r1);
+    const int C = chunk_cols(K);
+    for (int ra = r0; ra < r1; ra += 4) {
+        const int nr = min(4, r1 - ra);
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.empty[rg.slot], rg.ph ^ 1u, abort_flag, err, rg.lim)) return false;
+            const uint32_t fb = su32(&rg.full[rg.slot]);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(fb), "r"((uint32_t)(nr * C * 2))
+                         : "memory");
+            for (int j = 0; j < nr; j++)
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+                    "%4;" ::"r"(su32(rg.buf + (size_t)rg.slot * kPiece + (size_t)j * C * 2)),
+                    "l"(W + (size_t)(ra + j) * K + c0), "r"((uint32_t)(C * 2)), "r"(fb), "l"(policy)
+                    : "memory");
+            issued |= 1u << rg.slot;
+            last_ph = (last_ph & ~(1u << rg.slot)) | (rg.ph << rg.slot);
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+        }
+    }
+    return true;
+}
+
 template <int C>
-__device__ __noinline__ bool consume_narrow(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+__device__ __forceinline__ bool consume_c_r4(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+                                          volatile int *abort_flag, int *err) {
+    constexpr int PER_WARP = C / 8;
+    constexpr int STEPS = PER_WARP / 128;
+    static_assert(STEPS >= 1, "C >= 1024 (see consume_512)");
+    static_assert(4 == 4, "warp_sum4 reduces four rows");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cw = warp * PER_WARP + lane * 4;
+    for (int ra = r0; ra < r1; ra += 4) {
+        const int nr = min(4, r1 - ra);
+        float p[4][STEPS];
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int j = 0; j < STEPS; j++) p[r][j] = 0.f;
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err, rg.lim)) return false;
+            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
+            const float *xp = xs + c0 + cw;
+            float4 x[STEPS];
+            uint2 w[4][STEPS];
+#pragma unroll
+            for (int j = 0; j < STEPS; j++) {
+                x[j] = *reinterpret_cast<const float4 *>(xp + j * 128);
+#pragma unroll
+                for (int r = 0; r < 4; r++)
+                    w[r][j] = *reinterpret_cast<const uint2 *>(sa + (size_t)r * C * 2 + j * 256);
+            }
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+#pragma unroll
+            for (int j = 0; j < STEPS; j++)
+#pragma unroll
+                for (int r = 0; r < 4; r++) p[r][j] = dot4(w[r][j], x[j], p[r][j]);
+        }
+        float t[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            t[r] = 0.f;
+#pragma unroll
+            for (int j = 0; j < STEPS; j++) t[r] += p[r][j];
+        }
+        const float tot = warp_sum4(t[0], t[1], t[2], t[3]);
+        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
+    }
+    return true;
+}
+
+// C = 512 (K an odd multiple of 512, e.g. a tensor-parallel shard): warp w takes 64 columns of each
+// slot, lane l columns 2l, 2l+1
+__device__ __forceinline__ bool consume_512_r4(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
+                                            volatile int *abort_flag, int *err) {
+    constexpr int C = 512;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cw = warp * 64 + lane * 2;
+    for (int ra = r0; ra < r1; ra += 4) {
+        const int nr = min(4, r1 - ra);
+        float p[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = 0; c0 < K; c0 += C) {
+            if (!mb_wait(&rg.full[rg.slot], rg.ph, abort_flag, err, rg.lim)) return false;
+            const uint8_t *sa = rg.buf + (size_t)rg.slot * kPiece + (size_t)cw * 2;
+            const float2 x = *reinterpret_cast<const float2 *>(xs + c0 + cw);
+            uint32_t w[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) w[r] = *reinterpret_cast<const uint32_t *>(sa + (size_t)r * C * 2);
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&rg.empty[rg.slot])) : "memory");
+            if (++rg.slot == kRing) { rg.slot = 0; rg.ph ^= 1u; }
+#pragma unroll
+            for (int r = 0; r < 4; r++) p[r] = fmaf(bf16hi(w[r]), x.y, fmaf(bf16lo(w[r]), x.x, p[r]));
+        }
+        const float tot = warp_sum4(p[0], p[1], p[2], p[3]);
+        if ((lane & 7) == 0 && (lane >> 3) < nr) atomicAdd(acc + (ra - r0) + (lane >> 3), tot);
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool consume_r4(Ring &rg, int N, int K, const float *xs, float *acc, int &r0, int &r1,
+                                        volatile int *abort_flag, int *err) {
+    split_rows(N, blockIdx.x, gridDim.x, r0, r1);
+    const int tid = threadIdx.x;
+    for (int r = tid; r < r1 - r0; r += kStepConsumers) acc[r] = 0.f;
+    consumers_sync();
+    bool ok;
+    switch (chunk_cols(K)) {
+        case 4096: ok = consume_c_r4<4096>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 2048: ok = consume_c_r4<2048>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        case 1024: ok = consume_c_r4<1024>(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+        default: ok = consume_512_r4(rg, K, xs, acc, r0, r1, abort_flag, err); break;
+    }
+    if (!ok) return false;
+    consumers_sync();
+    return true;
+}
+
+// every CTA's writes before the barrier are visible to every CTA after it
+
+template <int C>
+__device__ __forceinline__ bool consume_narrow(Ring &rg, int K, const float *xs, float *acc, int r0, int r1,
                                             volatile int *abort_flag, int *err) {
     return consume_c<C>(rg, K, xs, acc, r0, r1, abort_flag, err);
 }
@@ -309,112 +436,86 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-// What the leader of each rank sends with its arrival at a cross-rank barrier.
-enum { PUB_NONE = 0, PUB_SS = 1 };
-
-// Barrier over every CTA of every tensor-parallel rank, in two levels:
-//   1. every CTA makes its stores into the peers' inboxes visible system-wide (fence.acq_rel.sys) and
-//      arrives at its own grid's counter;
-//   2. lanes 0..tp-1 of CTA 0's first warp wait for the whole grid, then write this rank's generation
-//      number into slot `rank` of every rank's flag array (one NVLink store per peer, no atomics);
-//   3. every CTA waits until the flag array of its own GPU shows the generation for every rank.
-// A rank's flag therefore stands for all of its CTAs.  Generations grow monotonically across barriers and
-// steps (a.gen persists) and are compared with wrap-around arithmetic.  PUB_SS: the q / k sums of squares
-// of the layer (accumulated in this grid by every CTA) travel in the same message, into slot `rank` of the
-// peers' sum arrays, so that every rank adds the tp slots in the same order and gets the same total.
-__device__ __forceinline__ bool cross_sync(const StepArgs &a, unsigned &target, unsigned &gen, int pub, int layer,
-                                           float sq, float sk, volatile int *abort_flag) {
-    consumers_sync();
-    const unsigned idx = target / gridDim.x;
-    target += gridDim.x;
-    gen += 1u;
-    const int tid = threadIdx.x;
-    if (tid == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 1] = trace_ns();
-    if (tid == 0) {
-        if (pub == PUB_SS) {
-            if (sq != 0.f) atomicAdd(a.ss + 2 * layer, sq);
-            if (sk != 0.f) atomicAdd(a.ss + 2 * layer + 1, sk);
-        }
-        fence_sys();  // this CTA's NVLink stores (ordered before by the named barrier) have landed
-        arrive(a, idx);
-    }
-    bool ok = true;
-    if (blockIdx.x == 0 && tid < 32) {
-        if (tid == 0) {
-            const uint64_t t0 = now_ns();
-            while (ld_acquire(a.bar) < target)
-                if (*abort_flag || now_ns() - t0 > a.wait_cycles) { ok = false; break; }
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok && tid < a.tp) {
-            unsigned *peer = a.xch[tid];
-            if (pub == PUB_SS) {
-                float *dst = reinterpret_cast<float *>(peer + kXSs) + 2 * a.rank;
-                dst[0] = __ldcg(a.ss + 2 * layer);
-                dst[1] = __ldcg(a.ss + 2 * layer + 1);
-            }
-            st_release_sys(peer + kXFlags + a.rank, gen);
-        }
-    }
-    if (ok && tid < a.tp) {
-        const unsigned *mine = a.xch[a.rank] + kXFlags + tid;
+// ---- tensor-parallel exchanges: flag-in-data words over NVLink, no fences ----
+// Every value a rank sends travels as one 8-byte word (fp32 bits | generation << 32), written with one
+// 64-bit store into the receiver's inbox and read with 64-bit loads: the store is single-copy atomic, so a
+// word that shows this exchange's generation carries this exchange's value, and the receiver needs no
+// barrier or fence to trust it.  Generations grow by one per exchange (identically on every rank, and
+// across steps through a.gen), so a slot never shows a stale word with the current generation.
+__device__ __forceinline__ unsigned long long ll_pack(float v, unsigned gen) {
+    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)gen << 32);
+}
+__device__ __forceinline__ void st_ll(unsigned *p, unsigned long long w) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll(const unsigned *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Wait (bounded) for the word at p to carry generation gen; its value, or false on expiry.
+__device__ __forceinline__ bool wait_ll(const StepArgs &a, const unsigned *p, unsigned gen, float &v,
+                                        volatile int *abort_flag) {
+    unsigned long long w = ld_ll(p);
+    if ((unsigned)(w >> 32) != gen) {
         const uint64_t t0 = now_ns();
-        while ((int)(ld_acquire_sys(mine) - gen) < 0)
-            if (*abort_flag || now_ns() - t0 > a.wait_cycles) { ok = false; break; }
+        do {
+            if (*abort_flag || now_ns() - t0 > a.wait_cycles) return false;
+            w = ld_ll(p);
+        } while ((unsigned)(w >> 32) != gen);
     }
-    if (!ok) {
-        *abort_flag = 1;
-        atomicExch(a.err, 4);
+    v = __uint_as_float((unsigned)w);
+    return true;
+}
+
+// this rank's partial of rows [r0, r1) of a row-split projection (O, down) into slot `rank` of every rank's
+// inbox `box` ([tp][D] words of 8 bytes)
+__device__ __forceinline__ void push_ll(const StepArgs &a, int box, int r0, int r1, const float *acc, unsigned gen) {
+    const int n = (r1 - r0) * a.tp;
+    for (int i = threadIdx.x; i < n; i += kStepConsumers) {
+        const int r = i / a.tp, p = i % a.tp;
+        st_ll(a.xch[p] + box + 2 * ((size_t)a.rank * a.D + r0 + r), ll_pack(acc[r], gen));
     }
-    if (tid == 0 && a.trace && blockIdx.x == 0) a.trace[2 * idx + 2] = trace_ns();
+}
+
+// The all-reduce of rows [r0, r1) (this CTA's rows of the projection): wait for every rank's partial of
+// them in this rank's inbox and add them, in rank order (the same sum on every rank), into the residual
+// stream x.  A grid barrier follows before any CTA reads x.
+__device__ __forceinline__ bool reduce_ll(const StepArgs &a, int box, int r0, int r1, float *x, unsigned gen,
+                                          float *scratch, volatile int *abort_flag, int *fail) {
+    const int n = (r1 - r0) * a.tp;
+    const unsigned *in = a.xch[a.rank] + box;
+    for (int i = threadIdx.x; i < n; i += kStepConsumers) {
+        const int r = i / a.tp, p = i % a.tp;
+        float v = 0.f;
+        if (!wait_ll(a, in + 2 * ((size_t)p * a.D + r0 + r), gen, v, abort_flag)) *fail = 1;
+        scratch[i] = v;
+    }
     consumers_sync();
-    return !*abort_flag;
-}
-
-// this rank's partial of rows [r0, r1) of a row-split projection into inbox slot `rank` of every rank
-__device__ __forceinline__ void push_partial(const StepArgs &a, int box, int r0, int r1, const float *acc) {
-    for (int r = threadIdx.x; r < r1 - r0; r += kStepConsumers) {
-        const float v = acc[r];
-        for (int p = 0; p < a.tp; p++)
-            reinterpret_cast<float *>(a.xch[p])[box + (size_t)a.rank * a.D + r0 + r] = v;
-    }
-}
-
-// xs = rmsnorm(x + sum over ranks of the inbox partials) * w; the rows this CTA owns of the
-// un-normalised sum are written to xnext (the residual stream's other buffer)
-__device__ __forceinline__ void load_resid(const StepArgs &a, float *xs, const float *xcur, int box, float *xnext,
-                                           const float *w, float *red) {
-    const int tid = threadIdx.x, K = a.D;
-    const float *in = reinterpret_cast<const float *>(a.xch[a.rank]) + box;
-    int o0, o1;
-    split_rows(K, blockIdx.x, gridDim.x, o0, o1);
-    float ss = 0.f;
-    for (int q = tid; q < (K >> 2); q += kStepConsumers) {
-        float4 v = __ldcg(reinterpret_cast<const float4 *>(xcur) + q);
-        for (int p = 0; p < a.tp; p++) {
-            const float4 t = __ldcg(reinterpret_cast<const float4 *>(in + (size_t)p * K) + q);
-            v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+    if (*fail) {
+        if (threadIdx.x == 0) {
+            *abort_flag = 1;
+            atomicExch(a.err, 4);
         }
-        reinterpret_cast<float4 *>(xs)[q] = v;
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        return false;
     }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    consumers_sync();
-    for (int k = o0 + tid; k < o1; k += kStepConsumers) xnext[k] = xs[k];
-    float tot = 0.f;
-#pragma unroll
-    for (int i = 0; i < kStepConsumerWarps; i++) tot += red[i];
-    const float sc = 1.0f / sqrtf(tot / (float)K + a.eps);
-    for (int q = tid; q < (K >> 2); q += kStepConsumers) {
-        float4 v = reinterpret_cast<float4 *>(xs)[q];
-        const float4 g = reinterpret_cast<const float4 *>(w)[q];
-        v.x = g.x * v.x * sc; v.y = g.y * v.y * sc; v.z = g.z * v.z * sc; v.w = g.w * v.w * sc;
-        reinterpret_cast<float4 *>(xs)[q] = v;
+    for (int r = threadIdx.x; r < r1 - r0; r += kStepConsumers) {
+        float t = __ldcg(x + r0 + r);
+        for (int p = 0; p < a.tp; p++) t += scratch[r * a.tp + p];
+        x[r0 + r] = t;
     }
-    consumers_sync();
+    return true;
+}
+
+// CTA 0 sends this rank's q / k sums of squares of the layer (complete after the QKV grid barrier) to every
+// rank: slot `rank` of their kXSs inbox ([tp][2] words)
+__device__ __forceinline__ void push_ss(const StepArgs &a, int layer, unsigned gen) {
+    if (blockIdx.x != 0 || threadIdx.x >= a.tp) return;
+    const float sq = __ldcg(a.ss + 2 * layer), sk = __ldcg(a.ss + 2 * layer + 1);
+    unsigned *dst = a.xch[threadIdx.x] + kXSs + 4 * a.rank;
+    st_ll(dst, ll_pack(sq, gen));
+    st_ll(dst + 2, ll_pack(sk, gen));
 }
 
 // xs = rmsnorm(src) * w over K elements (src read through L2); with w == nullptr a plain copy.
@@ -559,9 +660,9 @@ __device__ __forceinline__ void attn_mark(const StepArgs &a, int layer, int k) {
         a.trace[2 * (5 * a.layers + 1) + (size_t)layer * 8 + k] = trace_ns();
 }
 
-template <typename KT, int D, int G>
+template <typename KT, int D, int G, bool TPM>
 __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int kvh, int sp, int ns, float *sm,
-                          const KT *stage) {
+                          const KT *stage, unsigned ss_gen, volatile int *abort_flag) {
     constexpr int DPL = D / 32;
     constexpr int HALF = D / 2;
     using KV = SKV<KT, DPL>;
@@ -583,11 +684,27 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     float scq = 1.f, sck = 1.f;
     if (a.qk_mode == 1) {
         float tq = 0.f, tk = 0.f;
-        if (a.tp > 1) {  // every rank's sums, added in rank order (the same total on every rank)
-            const float *in = reinterpret_cast<const float *>(a.xch[a.rank] + kXSs);
+        if constexpr (TPM) {  // every rank's sums (flag-in-data words), added in rank order: the same total on every rank
+            __shared__ float ss_in[2 * 8];
+            __shared__ int ss_fail;
+            if (threadIdx.x == 0) ss_fail = 0;
+            consumers_sync();
+            if ((int)threadIdx.x < 2 * a.tp) {
+                float v = 0.f;
+                if (!wait_ll(a, a.xch[a.rank] + kXSs + 2 * threadIdx.x, ss_gen, v, abort_flag)) ss_fail = 1;
+                ss_in[threadIdx.x] = v;
+            }
+            consumers_sync();
+            if (ss_fail) {
+                if (threadIdx.x == 0) {
+                    *abort_flag = 1;
+                    atomicExch(a.err, 4);
+                }
+                return;
+            }
             for (int p = 0; p < a.tp; p++) {
-                tq += __ldcg(in + 2 * p);
-                tk += __ldcg(in + 2 * p + 1);
+                tq += ss_in[2 * p];
+                tk += ss_in[2 * p + 1];
             }
         } else {
             tq = __ldcg(a.ss + 2 * layer);
@@ -887,11 +1004,24 @@ __device__ void attn_item(const StepArgs &a, const StepLayer &Ly, int layer, int
     }
 }
 
+template <bool TPM>
+__device__ __forceinline__ bool produce_t(Ring &rg, const __nv_bfloat16 *W, int N, int K, volatile int *abort_flag,
+                                          int *err, uint32_t &issued, uint32_t &last_ph, uint64_t policy) {
+    if constexpr (TPM) return produce(rg, W, N, K, abort_flag, err, issued, last_ph, policy);
+    else return produce_r4(rg, W, N, K, abort_flag, err, issued, last_ph, policy);
+}
+template <bool TPM>
+__device__ __forceinline__ bool consume_t(Ring &rg, int N, int K, const float *xs, float *acc, int &r0, int &r1,
+                                          volatile int *abort_flag, int *err) {
+    if constexpr (TPM) return consume(rg, N, K, xs, acc, r0, r1, abort_flag, err);
+    else return consume_r4(rg, N, K, xs, acc, r0, r1, abort_flag, err);
+}
+
 template <typename KT, int D, int G, bool TPM>
 __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kRing], empty_bar[kRing];
-    __shared__ int abort_sh;
+    __shared__ int abort_sh, xfail;
     __shared__ float red[kStepConsumerWarps], red2[kStepConsumerWarps];
     __shared__ float am_v[kStepConsumers];
     __shared__ int am_i[kStepConsumers];
@@ -909,6 +1039,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
                          : "memory");
         }
         abort_sh = 0;
+        xfail = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -929,12 +1060,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
                 asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(policy));
             for (int l = 0; l < a.layers && ok; l++) {
                 const StepLayer &Ly = a.L[l];
-                ok = ok && produce(rg, Ly.w_qkv, QKV, D_, abort_flag, a.err, issued, last_ph, policy);
-                ok = ok && produce(rg, Ly.w_o, D_, Q, abort_flag, a.err, issued, last_ph, policy);
-                ok = ok && produce(rg, Ly.w_gu, 2 * F, D_, abort_flag, a.err, issued, last_ph, policy);
-                ok = ok && produce(rg, Ly.w_down, D_, F, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce_t<TPM>(rg, Ly.w_qkv, QKV, D_, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce_t<TPM>(rg, Ly.w_o, D_, Q, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce_t<TPM>(rg, Ly.w_gu, 2 * F, D_, abort_flag, a.err, issued, last_ph, policy);
+                ok = ok && produce_t<TPM>(rg, Ly.w_down, D_, F, abort_flag, a.err, issued, last_ph, policy);
             }
-            ok = ok && produce(rg, a.lm, a.V, D_, abort_flag, a.err, issued, last_ph, policy);
+            ok = ok && produce_t<TPM>(rg, a.lm, a.V, D_, abort_flag, a.err, issued, last_ph, policy);
             if (!ok) {
                 for (int i = 0; i < kRing; i++)
                     if (issued >> i & 1u) {
@@ -954,8 +1085,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
     int r0, r1;
     const int token = *a.tokens;
     constexpr bool tpm = TPM;  // tensor parallel: compiled only into the tp > 1 variants
-    const int box_o = kXRows, box_d = kXRows + a.tp * D_;
-    float *xcur = a.x, *xnext = a.x2;  // residual stream (ping-pong under tensor parallelism)
+    const int box_o = kXRows, box_d = kXRows + 2 * a.tp * D_;  // inboxes of [tp][D] 8-byte words
+    float *xcur = a.x;  // residual stream (updated in place by the owner of each row)
     if (a.trace && blockIdx.x == 0 && tid == 0) a.trace[0] = trace_ns();
     for (int l = 0; l < a.layers; l++) {
         const StepLayer &Ly = a.L[l];
@@ -979,9 +1110,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
             const float sc = 1.0f / sqrtf(tot / (float)D_ + a.eps);
             for (int k = tid; k < D_; k += kStepConsumers) xs[k] = Ly.rms_att[k] * xs[k] * sc;
             consumers_sync();
-        } else if (tpm) {
-            load_resid(a, xs, xcur, box_d, xnext, Ly.rms_att, red);
-            float *t = xcur; xcur = xnext; xnext = t;
         } else {
             load_vec(xs, xcur, D_, Ly.rms_att, a.eps, red);
         }
@@ -996,7 +1124,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
                 if (t0 < t1) stage_kv<KT, D>(a, Ly, kvh, t0, t1, n - 1, stage);
             }
         }
-        if (!consume(rg, QKV, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
+        if (!consume_t<TPM>(rg, QKV, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
         {
             // the QKV rows, and the sums of squares of the q and k rows for the whole-vector QK-norm
             float sq = 0.f, sk = 0.f;
@@ -1015,61 +1143,55 @@ __global__ void __launch_bounds__(kStepThreads, 1) qw_step_kernel(const StepArgs
                 for (int w = 0; w < kStepConsumerWarps; w++) { tq += red[w]; tk += red2[w]; }
                 sq = tq;
                 sk = tk;
-                if (tid == 0 && !tpm) {
+                if (tid == 0) {
                     if (tq != 0.f) atomicAdd(a.ss + 2 * l, tq);
                     if (tk != 0.f) atomicAdd(a.ss + 2 * l + 1, tk);
                 }
             }
-            if (tpm && a.qk_mode == 1) {
-                if (!cross_sync(a, target, gen, PUB_SS, l, sq, sk, abort_flag)) break;
-            } else if (!grid_sync(a, target, abort_flag)) {
-                break;
-            }
+            if (!grid_sync(a, target, abort_flag)) break;
+            if (tpm && a.qk_mode == 1) push_ss(a, l, ++gen);  // the layer's sums, complete after the barrier
         }
         // ---- attention (this rank's heads) ----
         {
             const int n = *a.positions + 1;
             const int ns = attn_splits(gridDim.x, a.Hkv, n);
             if ((int)blockIdx.x < a.Hkv * ns)
-                attn_item<KT, D, G>(a, Ly, l, blockIdx.x / ns, blockIdx.x % ns, ns, scratch, stage);
+                attn_item<KT, D, G, TPM>(a, Ly, l, blockIdx.x / ns, blockIdx.x % ns, ns, scratch, stage, gen, abort_flag);
         }
         if (!grid_sync(a, target, abort_flag)) break;
         // ---- O projection + residual (summed over ranks through the inboxes) ----
         load_vec(xs, a.attn, Q, nullptr, 0.f, red);
-        if (!consume(rg, D_, Q, xs, acc, r0, r1, abort_flag, a.err)) break;
-        if (tpm) {
-            push_partial(a, box_o, r0, r1, acc);
-            if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
-            load_resid(a, xs, xcur, box_o, xnext, Ly.rms_ffn, red);
-            float *t = xcur; xcur = xnext; xnext = t;
+        if (!consume_t<TPM>(rg, D_, Q, xs, acc, r0, r1, abort_flag, a.err)) break;
+        if (tpm) {  // all-reduce of this CTA's rows over the ranks, into the residual stream
+            push_ll(a, box_o, r0, r1, acc, ++gen);
+            if (!reduce_ll(a, box_o, r0, r1, xcur, gen, xs, abort_flag, &xfail)) break;
         } else {
             for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
-            if (!grid_sync(a, target, abort_flag)) break;
-            load_vec(xs, xcur, D_, Ly.rms_ffn, a.eps, red);
         }
+        if (!grid_sync(a, target, abort_flag)) break;
+        load_vec(xs, xcur, D_, Ly.rms_ffn, a.eps, red);
         // ---- gate/up (raw) ----
-        if (!consume(rg, 2 * F, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
+        if (!consume_t<TPM>(rg, 2 * F, D_, xs, acc, r0, r1, abort_flag, a.err)) break;
         for (int r = tid; r < r1 - r0; r += kStepConsumers) a.gu[r0 + r] = acc[r];
         if (!grid_sync(a, target, abort_flag)) break;
         // ---- SwiGLU (rows interleaved 16 gate / 16 up) + down + residual ----
         load_swiglu(xs, a.gu, F);
-        if (!consume(rg, D_, F, xs, acc, r0, r1, abort_flag, a.err)) break;
+        if (!consume_t<TPM>(rg, D_, F, xs, acc, r0, r1, abort_flag, a.err)) break;
         if (tpm) {
-            push_partial(a, box_d, r0, r1, acc);
-            if (!cross_sync(a, target, gen, PUB_NONE, l, 0.f, 0.f, abort_flag)) break;
+            push_ll(a, box_d, r0, r1, acc, ++gen);
+            if (!reduce_ll(a, box_d, r0, r1, xcur, gen, xs, abort_flag, &xfail)) break;
         } else {
             for (int r = tid; r < r1 - r0; r += kStepConsumers) xcur[r0 + r] = __ldcg(xcur + r0 + r) + acc[r];
-            if (!grid_sync(a, target, abort_flag)) break;
         }
+        if (!grid_sync(a, target, abort_flag)) break;
     }
     if (*abort_flag) {
         asm volatile("cp.async.wait_all;" ::: "memory");  // staged attention keys still in flight
         return;
     }
     // ---- final rmsnorm + lm_head (this rank's vocabulary rows) + argmax ----
-    if (tpm) load_resid(a, xs, xcur, box_d, xnext, a.norm_final, red);
-    else load_vec(xs, xcur, D_, a.norm_final, a.eps, red);
-    if (!consume(rg, a.V, D_, xs, acc, r0, r1, abort_flag, a.err)) return;
+    load_vec(xs, xcur, D_, a.norm_final, a.eps, red);
+    if (!consume_t<TPM>(rg, a.V, D_, xs, acc, r0, r1, abort_flag, a.err)) return;
     if (a.trace && blockIdx.x == 0 && tid == 0) a.trace[2 * (target / gridDim.x) + 1] = trace_ns();
     float bv = -FLT_MAX;
     int bi = INT_MAX;
