@@ -271,7 +271,8 @@ def parity_check(rank, world, local, share_id, decode_kernels=0):
     """Before anything is timed, at every GPU count: the tensor-parallel model over `world` ranks against the
     oracle's answers (committed fixture).  fp32 mode: logits at the 8 prompt positions within 1e-3 relative
     L2.  bf16 mode (the decode path the bench times): the oracle's 40 tokens fed one per step, every logits
-    row within 2e-2 relative L2 and every greedy choice after the prompt identical."""
+    row within 2e-2 relative L2 and every greedy choice after the prompt identical; and the batched
+    tensor-core path (batch 8) generating the same 32 greedy tokens in every sequence."""
     import numpy as np
     from common_b200 import native
     fx = np.load(os.path.join(ROOT, "tests", "golden", "tp_parity.npz"))
@@ -309,7 +310,20 @@ def parity_check(rank, world, local, share_id, decode_kernels=0):
             out["bf16_token_mismatches"] = bad
             out["bf16_launches_per_token"] = m.last_launch_count
         m.close()
-    out["ok"] = bool(out["fp32_max_rel_l2"] < 1e-3 and out["bf16_max_rel_l2"] < 2e-2 and not out["bf16_token_mismatches"])
+    # the batched tensor-core path (tcgen05 prefill of 8 copies of the prompt, then batch-8 greedy decode
+    # through qw_generate): every sequence must produce the oracle's tokens
+    cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
+                             g["vocab"], g["seq_len"], False, native.QKNORM_VECTOR, False, native.DTYPE_BF16,
+                             native.DTYPE_BF16, 8, 64)
+    m = native.NativeModel(cfg, local, rank, world, share_id(native.unique_id))
+    m.init_synthetic(seed, std)
+    m.finalize()
+    toks = fx["bf16_tokens"]
+    got = m.generate(np.repeat(fx["prompt"][None].astype(np.int32), 8, 0), len(toks))
+    m.close()
+    out["batched_b8_token_mismatches"] = sorted({int(p) for b in range(8) for p in np.nonzero(got[b] != toks)[0]})
+    out["ok"] = bool(out["fp32_max_rel_l2"] < 1e-3 and out["bf16_max_rel_l2"] < 2e-2 and not out["bf16_token_mismatches"]
+                     and not out["batched_b8_token_mismatches"])
     return out
 
 
@@ -565,6 +579,7 @@ def run_case(args):
       step-small  the 8B geometry cut to --layers layers, 4 batch-1 decode steps (the persistent step kernel)
       gemm        one qw_op_linear GEMM (--gemm M K T EPI) timed with CUDA events
       attn-b64    the 8B geometry cut to 2 layers, 64 sequences prefilled to 2048 tokens, 3 batch-64 decode steps
+      prefill-small  the 8B geometry cut to 2 layers, two prefills of 8 x 4096 tokens
     """
     import numpy as np
     from common_b200 import build, native
@@ -593,6 +608,21 @@ def run_case(args):
         ms = e0.elapsed_time(e1) / 10
         print(json.dumps({"case": "gemm", "M": M, "K": K, "T": T, "epi": epi, "ms": ms,
                           "tflops": 2.0 * M * K * T / ms / 1e9}))
+        return 0
+    if args.case == "prefill-small":
+        # the 8B geometry cut to 2 layers, one prefill of 8 x 4096 tokens (tcgen05 GEMMs + tcgen05 attention)
+        cfg = native.make_config(g["dim"], g["hidden_dim"], 2, g["heads"], g["kv_heads"], g["head_dim"], g["vocab"],
+                                 4096 + 16, False, native.QKNORM_VECTOR, False, native.DTYPE_BF16, native.DTYPE_BF16,
+                                 8, 32768)
+        m = native.NativeModel(cfg, 0)
+        m.init_synthetic(0, 0.02)
+        m.finalize()
+        prompts = np.random.default_rng(1).integers(0, g["vocab"], (8, 4096)).astype(np.int32)
+        for _ in range(2):
+            m.prefill(prompts, want_logits=False)
+        m.synchronize()
+        m.close()
+        print(json.dumps({"case": args.case, "ok": True}))
         return 0
     layers = args.layers if args.case == "step-small" else 2
     B, L = (1, 1024) if args.case == "step-small" else (64, 2048)
@@ -632,7 +662,7 @@ def main():
     ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--decode-batch", type=int, default=64)
     ap.add_argument("--batch-steps", type=int, default=32)
-    ap.add_argument("--case", choices=["step-small", "gemm", "attn-b64"], help="a small profiler workload instead")
+    ap.add_argument("--case", choices=["step-small", "gemm", "attn-b64", "prefill-small"], help="a small profiler workload instead")
     ap.add_argument("--layers", type=int, default=4, help="--case step-small: layers of the cut 8B model")
     ap.add_argument("--gemm", type=int, nargs=4, default=[24576, 4096, 4096, 2], metavar=("M", "K", "T", "EPI"))
     ap.add_argument("--no-cpu-baseline", action="store_true")

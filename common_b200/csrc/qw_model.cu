@@ -983,9 +983,9 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
         }
         AL(m->gu_split, (size_t)B * 2 * m->Fl);
     }
-    // the persistent step kernel: automatic at tp 1; under tensor parallelism only when asked for
-    // (decode_kernels 2), its cross-GPU barriers cost more than the NCCL path saves at these sizes
-    if (m->bf16w && (c.decode_kernels == 2 || (c.decode_kernels == 0 && tp_size == 1))) {
+    // the persistent step kernel for batch-1 decode with bf16 weights at any tp (decode_kernels 0 or 2) when the
+    // geometry fits it; under tensor parallelism its all-reduces are flag-in-data exchanges over NVLink
+    if (m->bf16w && c.decode_kernels != 1) {
         StepArgs &sa = m->step;
         sa.layers = c.layers; sa.D = D; sa.F = m->Fl; sa.V = m->Vl; sa.H = m->Hl; sa.Hkv = m->Hkvl; sa.d = c.head_dim;
         sa.kv_bf16 = m->bf16kv;

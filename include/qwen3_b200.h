@@ -76,10 +76,10 @@ typedef struct qw_config {
     int32_t max_tokens;     /* max tokens in one prefill call (activation arena), >= max_batch */
     int32_t page_size;      /* KV page size in tokens (power of two, 16..256); 0 = 64 */
     int32_t num_pages;      /* KV pages per rank; 0 = max_batch * ceil(seq_len / page_size) */
-    int32_t decode_kernels; /* batch-1 decode with bf16 weights: 0 = auto (one persistent kernel per step at
-                               tp 1, one kernel per operation + NCCL under tensor parallelism), 1 = one
-                               kernel per operation, 2 = the persistent kernel at any tp (cross-GPU
-                               exchange over NVLink peer memory) */
+    int32_t decode_kernels; /* batch-1 decode with bf16 weights: 0 = auto (one persistent kernel per step when the
+                               geometry fits it, at any tp: its cross-GPU all-reduces are flag-in-data stores
+                               into the peers' memory over NVLink), 1 = one kernel per operation (+ NCCL under
+                               tensor parallelism), 2 = the persistent kernel (as 0) */
     int32_t wait_limit_us;  /* bound of every device-side wait (grid and cross-GPU barriers, copies in flight,
                                split merges) in microseconds; 0 = 2 s.  A wait that runs out stops the kernel,
                                which records the site; qw_synchronize then returns QW_ERR_TIMEOUT */

@@ -66,31 +66,23 @@ def test_tc_batched_decode_matches_oracle():
 
 
 def test_tc_generate_batch_greedy_matches_oracle():
-    """Batched prefill + device-resident greedy loop over the tensor-core decode path, checked step by
-    step: the oracle is fed the device's own tokens and at every generated step its argmax must be the
-    device's token, or the two must be a near-tie of the oracle's logits (gap below 2e-2 of the logits'
-    standard deviation -- the bf16 activations of the tensor-core path can swap such a pair)."""
-    c = cfg_dict(seq_len=64, vocab=500)
-    sd = state_dict(c, seed=25, std=0.08, norm_noise=0.1)
-    B, P, N = 6, 8, 32
-    prompts = np.random.default_rng(26).integers(0, c["vocab"], (B, P)).astype(np.int32)
-    m = native_model(c, sd, precision="bf16", max_batch=B, max_tokens=B * P)
-    got = m.generate(prompts, P + N)
-    exact = 0
-    for b in range(B):
-        np.testing.assert_array_equal(got[b, :P], prompts[b])
-        o = oracle_model(c, sd, bf16_weights=True)
-        for p in range(P + N - 1):
-            lg = o.forward_token(int(got[b, p]), p)
-            if p < P - 1:
-                continue
-            dev_tok, best = int(got[b, p + 1]), int(np.argmax(lg))
-            if dev_tok == best:
-                exact += 1
-            else:
-                assert lg[best] - lg[dev_tok] < 2e-2 * lg.std(), (b, p, lg[best] - lg[dev_tok], lg.std())
-        o.close()
-    assert exact >= 0.9 * B * N, exact
+    """Batched prefill + device-resident greedy loop over the tensor-core decode path: six sequences of the
+    parity fixture's prompt (tests/golden/tp_parity.npz: N(0, 0.02) synthetic weights, norms 1, a seed whose
+    greedy choices all have margins far above the bf16 error) must generate exactly the oracle's 32 tokens."""
+    from common_b200 import native
+    from tests.tp_worker import parity_fixture
+    g, fx = parity_fixture()
+    cfg = native.make_config(g["dim"], g["hidden_dim"], g["layers"], g["heads"], g["kv_heads"], g["head_dim"],
+                             g["vocab"], g["seq_len"], False, native.QKNORM_VECTOR, False, native.DTYPE_BF16,
+                             native.DTYPE_BF16, 6, 48)
+    m = native.NativeModel(cfg, 0)
+    m.init_synthetic(int(fx["seed"]), float(fx["std"]))
+    m.finalize()
+    toks = fx["bf16_tokens"]
+    got = m.generate(np.repeat(fx["prompt"][None].astype(np.int32), 6, 0), len(toks))
+    m.close()
+    for b in range(6):
+        np.testing.assert_array_equal(got[b], toks)
 
 
 def test_tc_prefill_8b_layer_geometry():
