@@ -125,6 +125,15 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t *r) {
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 __global__ void __launch_bounds__(kAtThreads, 1)
     qw_flash_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV, const AtParams a) {
@@ -293,20 +302,19 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             for (int c = 0; c < 4; c++) tmem_ld32_nw(ts + (uint32_t)(c * 32), v + c * 32);
             tmem_wait_ld();
             const int kbase = j * kAtKeys;
-            float mx = -INFINITY;
+            // maximum of the raw scores (the scale is positive), 4 independent chains
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (kbase + kAtKeys - 1 > pos) {
 #pragma unroll
                 for (int e = 0; e < kAtKeys; e++) {
-                    v[e] = kbase + e <= pos ? v[e] * a.sl2 : -INFINITY;
-                    mx = fmaxf(mx, v[e]);
+                    if (kbase + e > pos) v[e] = -INFINITY;
+                    m4[e & 3] = fmaxf(m4[e & 3], v[e]);
                 }
             } else {
 #pragma unroll
-                for (int e = 0; e < kAtKeys; e++) {
-                    v[e] *= a.sl2;
-                    mx = fmaxf(mx, v[e]);
-                }
+                for (int e = 0; e < kAtKeys; e++) m4[e & 3] = fmaxf(m4[e & 3], v[e]);
             }
+            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * a.sl2;
             float alpha = 1.f;
             bool need = false;
             if (j == 0) {
@@ -316,14 +324,21 @@ __global__ void __launch_bounds__(kAtThreads, 1)
                 m_use = mx;
                 need = true;
             }
-            float sum = 0.f;
-            uint32_t pk[kAtKeys / 2];
+            // p = 2^(s * scale * log2 e - m): one FMA and one ex2 per score; P_t(j) goes to TMEM as packed bf16
+            // pairs over the first 64 columns of S_t(j), 16 columns (32 scores) at a time
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int e = 0; e < kAtKeys; e += 2) {
-                const float p0 = ex2(v[e] - m_use), p1 = ex2(v[e + 1] - m_use);
-                sum += p0 + p1;
-                pk[e / 2] = pack2(p0, p1);
+            for (int c = 0; c < 4; c++) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float p0 = ex2(fmaf(v[c * 32 + e], a.sl2, -m_use)), p1 = ex2(fmaf(v[c * 32 + e + 1], a.sl2, -m_use));
+                    s4[(e >> 1) & 3] += p0 + p1;
+                    pk[e / 2] = pack2(p0, p1);
+                }
+                tmem_st16u(ts + (uint32_t)(c * 16), pk);
             }
+            const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
             l = l * alpha + sum;
             // O_t: PV_t(j - 1) has completed (s_full of this block was committed after it)
             if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -337,9 +352,6 @@ __global__ void __launch_bounds__(kAtThreads, 1)
                     tmem_st32(to + (uint32_t)(c * 32), o);
                 }
             }
-            // P_t(j) as packed bf16 pairs over the first 64 columns of S_t(j)
-            tmem_st32u(ts, pk);
-            tmem_st32u(ts + 32u, pk + 32);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
