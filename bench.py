@@ -394,8 +394,14 @@ def run_decode_config(name, g, B, prompt_len, gen, rank, world, local, nid, peak
     step_bytes = wb["layers_total"] + wb["lm_head"] + B * kv_bytes_per_token(g, ctx_mid, world)
     gbs = step_bytes / (ms / steps * 1e-3) / 1e9
     peak = peaks.get("hbm_gbs", 6650.0)
+    # per-kernel split of one eager step (CUDA events around every launch)
+    m.set_device_inputs(dt.cpu().numpy(), dp.cpu().numpy())
+    kd, kk = m.profile_decode(B)
+    kern = {}
+    for x, k in zip(kd, kk):
+        kern[native.KERNEL_NAMES[int(k)]] = kern.get(native.KERNEL_NAMES[int(k)], 0.0) + float(x)
     m.close()
-    return {"workload": name, "tok_s": B * steps / (ms * 1e-3), "ms_per_step": ms / steps, "batch": B,
+    return {"kernel_ms_per_step": kern, "workload": name, "tok_s": B * steps / (ms * 1e-3), "ms_per_step": ms / steps, "batch": B,
             "prompt_len": prompt_len, "generated": gen, "timed_steps": steps, "warmup_steps": warm,
             "context": [prompt_len + warm, prompt_len + gen], "launches_per_step": launches, "parallelism": f"tp{world}",
             "prefill_s": prefill_s,
@@ -416,8 +422,9 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     build.build()
     from common_b200 import parallel
-    parity = parity_check(rank, world, local, parallel.share_unique_id, args.decode_kernels)
-    if not parity["ok"]:
+    parity = None if args.no_parity else parity_check(rank, world, local, parallel.share_unique_id,
+                                                          args.decode_kernels)
+    if parity and not parity["ok"]:
         print(json.dumps({"parity_failed": parity}), file=sys.stderr, flush=True)
     nid = parallel.share_unique_id(native.unique_id)  # one NCCL id per communicator (per model)
     g = GEOM_8B
@@ -666,6 +673,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4, help="--case step-small: layers of the cut 8B model")
     ap.add_argument("--gemm", type=int, nargs=4, default=[24576, 4096, 4096, 2], metavar=("M", "K", "T", "EPI"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity gate (profiler runs only)")
     ap.add_argument("--no-configs", action="store_true", help="skip the configs[1] (1 GPU) / configs[4] (8 GPUs) legs")
     ap.add_argument("--decode-kernels", type=int, default=0,
                     help="batch-1 decode path: 0 auto, 1 one kernel per operation, 2 the persistent step kernel")
