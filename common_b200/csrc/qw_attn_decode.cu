@@ -350,6 +350,8 @@ static cudaError_t attn_launch_g(const AttnArgs &a, int G, dim3 grid, cudaStream
         case 1: qw_attn_decode_kernel<KT, D, 1><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
         case 2: qw_attn_decode_kernel<KT, D, 2><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
         case 4: qw_attn_decode_kernel<KT, D, 4><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
+        case 6: qw_attn_decode_kernel<KT, D, 6><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
+        case 7: qw_attn_decode_kernel<KT, D, 7><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
         case 8: qw_attn_decode_kernel<KT, D, 8><<<grid, kAttnWarps * 32, 0, st>>>(a); break;
         default: return cudaErrorInvalidValue;
     }

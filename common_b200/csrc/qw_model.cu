@@ -576,7 +576,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             fa.seq_slots = seq_slots; fa.p0 = p0; fa.L = L; fa.H = m->Hl; fa.Hkv = m->Hkvl; fa.d = d;
             fa.scale = (float)(1.0 / sqrt((double)d)); fa.out = pf.act; fa.ld_out = m->Ql;
             fa.num_pages = m->num_pages; fa.err = pf.d_err;
-            if (d == 128 && m->tc_attn) LKK(QW_KERNEL_ATTN, flash_prefill_tc_launch(fa, nseq, m->st));
+            if (d == 128 && m->tc_attn && !(m->Hl / m->Hkvl & (m->Hl / m->Hkvl - 1))) LKK(QW_KERNEL_ATTN, flash_prefill_tc_launch(fa, nseq, m->st));
             else LKK(QW_KERNEL_ATTN, flash_prefill_launch(fa, nseq, m->st));
         } else {
             FlashDecodeArgs fd{};
@@ -870,7 +870,8 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
     if (c.head_dim != 64 && c.head_dim != 128) return fail(m, QW_ERR_UNSUPPORTED, "head_dim %d (64 or 128)", c.head_dim);
     if (c.heads % c.kv_heads) return fail(m, QW_ERR_SHAPE, "heads %d not a multiple of kv_heads %d", c.heads, c.kv_heads);
     int G = c.heads / c.kv_heads;
-    if (G != 1 && G != 2 && G != 4 && G != 8) return fail(m, QW_ERR_UNSUPPORTED, "heads per kv group %d", G);
+    if (G < 1 || G > 8 || G == 3 || G == 5)
+        return fail(m, QW_ERR_UNSUPPORTED, "heads per kv group %d (1, 2, 4, 6, 7 or 8)", G);
     if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return fail(m, QW_ERR_ARG, "tp rank/size %d/%d", tp_rank, tp_size);
     if (c.kv_heads % tp_size || c.vocab % tp_size || c.hidden_dim % (kGuBlock * tp_size))
         return fail(m, QW_ERR_SHAPE, "kv_heads, vocab and hidden_dim/16 must divide by tp=%d", tp_size);
@@ -886,6 +887,7 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
     m->log2_page = 0;
     while ((1 << m->log2_page) < m->page_size) m->log2_page++;
     m->dev = device; m->rank = tp_rank; m->tp = tp_size;
+    cudaGetLastError();  // an earlier, unrelated failure of this thread must not be reported as ours
 
     m->bf16w = c.weight_dtype == QW_DTYPE_BF16; m->wsz = m->bf16w ? 2 : 4;
     m->bf16kv = c.kv_dtype == QW_DTYPE_BF16; m->kvsz = m->bf16kv ? 2 : 4;
@@ -1531,6 +1533,7 @@ void qw_destroy(qw_model *m) {
     prefill_free(m->pf);
     if (m->comm) ncclCommDestroy(m->comm);
     if (m->st) cudaStreamDestroy(m->st);
+    cudaGetLastError();  // a failed release leaves no error for the next call of this thread to report
     delete m;
 }
 

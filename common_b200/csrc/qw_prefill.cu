@@ -590,6 +590,8 @@ static cudaError_t flash_decode_g(const FlashDecodeArgs &a, dim3 grid, cudaStrea
         case 1: return launch_pdl(qw_flash_decode_kernel<D, 1>, grid, block, smem, st, a);
         case 2: return launch_pdl(qw_flash_decode_kernel<D, 2>, grid, block, smem, st, a);
         case 4: return launch_pdl(qw_flash_decode_kernel<D, 4>, grid, block, smem, st, a);
+        case 6: return launch_pdl(qw_flash_decode_kernel<D, 6>, grid, block, smem, st, a);
+        case 7: return launch_pdl(qw_flash_decode_kernel<D, 7>, grid, block, smem, st, a);
         case 8: return launch_pdl(qw_flash_decode_kernel<D, 8>, grid, block, smem, st, a);
         default: return cudaErrorInvalidValue;
     }
@@ -648,6 +650,8 @@ cudaError_t prefill_kernels_prepare() {
                          (const void *)qw_flash_prefill_kernel<64>,
                          (const void *)qw_flash_decode_kernel<128, 1>, (const void *)qw_flash_decode_kernel<128, 2>,
                          (const void *)qw_flash_decode_kernel<128, 4>, (const void *)qw_flash_decode_kernel<128, 8>,
+                         (const void *)qw_flash_decode_kernel<128, 6>, (const void *)qw_flash_decode_kernel<128, 7>,
+                         (const void *)qw_flash_decode_kernel<64, 6>, (const void *)qw_flash_decode_kernel<64, 7>,
                          (const void *)qw_flash_decode_kernel<64, 1>, (const void *)qw_flash_decode_kernel<64, 2>,
                          (const void *)qw_flash_decode_kernel<64, 4>, (const void *)qw_flash_decode_kernel<64, 8>};
     for (const void *f : fns) {

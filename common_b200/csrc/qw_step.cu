@@ -27,7 +27,7 @@ bool step_layout(StepArgs &a, int grid, size_t *smem_out) {
     const int Q = a.H * a.d, KVw = a.Hkv * a.d, G = a.H / a.Hkv;
     if (a.D % 512 || Q % 512 || a.F % 512) return false;
     if (a.d != 64 && a.d != 128) return false;
-    if (G != 1 && G != 2 && G != 4 && G != 8) return false;
+    if (G < 1 || G > 8 || G == 3 || G == 5) return false;
     a.max_k = std::max(a.D, std::max(Q, a.F));
     // staged keys sit above both the QKV phase's activation vector and the attention scratch
     a.stage_off = (int)((std::max((size_t)a.D, attn_floats(a.d, G)) + 31) & ~(size_t)31);

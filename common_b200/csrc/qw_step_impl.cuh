@@ -1295,6 +1295,8 @@ const void *step_fn_g(int G) {
         case 1: return (const void *)qw_step_kernel<KT, D, 1, TPM>;
         case 2: return (const void *)qw_step_kernel<KT, D, 2, TPM>;
         case 4: return (const void *)qw_step_kernel<KT, D, 4, TPM>;
+        case 6: return (const void *)qw_step_kernel<KT, D, 6, TPM>;
+        case 7: return (const void *)qw_step_kernel<KT, D, 7, TPM>;
         case 8: return (const void *)qw_step_kernel<KT, D, 8, TPM>;
     }
     return nullptr;
