@@ -14,6 +14,7 @@
 //             AggregationFeatures.java:111-121, reduced by the last CTA to finish).
 // The roofline is HBM bandwidth: algorithmic bytes = N*K*sizeof(WT) per launch.
 #include "qw_internal.cuh"
+#include "qw_ops.h"
 #include <float.h>
 #include <limits.h>
 #include <map>
@@ -324,6 +325,8 @@ static int prepare_cached(const void *fn, size_t smem, cudaError_t *err) {
     }
     int occ = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kGemvThreads, smem) != cudaSuccess || occ < 1) occ = 1;
+    // the argmax epilogue's cross-CTA scratch (qw_ops.cu, qw_noalloc.cu) is sized for this many CTAs per SM
+    if (occ > kGemvMaxCtasPerSm) occ = kGemvMaxCtasPerSm;
     cache[{fn, smem}] = occ;
     return occ;
 }

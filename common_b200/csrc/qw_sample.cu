@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kSampThreads) qw_sample_rows_kernel(SampleArgs
     __shared__ double hist_m[2048];
     __shared__ int s_pick;
     __shared__ double s_r;
-    __shared__ unsigned long long s_sel;
+    __shared__ unsigned long long s_sel, s_cum;
     const int row = blockIdx.x, tid = threadIdx.x;
     const float *lg = a.logits + (size_t)row * a.ld;
     double *q = a.scratch + (size_t)row * a.V;
@@ -130,38 +130,45 @@ __global__ void __launch_bounds__(kSampThreads) qw_sample_rows_kernel(SampleArgs
         unsigned long long cut = 0;  // elements with bit pattern > cut are kept; == cut kept up to `ties`
         long long ties = -1;         // -1: no filtering
         if (a.mode == 1 && a.top_p < 1.0) {
+            // probability mass in 2^-60 fixed point: integer atomics add in any order to the same total, so
+            // the cutoff does not depend on the order in which threads arrive (the sum's rounding, at most
+            // V x 2^-61 ~ 1e-13, is below any gap the comparison with top_p could resolve in double)
+            constexpr double kFix = 1152921504606846976.0;  // 2^60
+            unsigned long long *hist_u = reinterpret_cast<unsigned long long *>(hist_m);
+            const unsigned long long top_u = __double2ull_rn(a.top_p * kFix);
             unsigned long long prefix = 0;
-            double above = 0.0;  // mass of the elements whose pattern is above the current prefix range
+            unsigned long long above_u = 0;  // mass of the elements whose pattern is above the current prefix range
             const int widths[6] = {11, 11, 11, 11, 10, 10};
             int shift = 64;
             for (int pass = 0; pass < 6; pass++) {
                 const int w = widths[pass];
                 shift -= w;
                 const int nb = 1 << w;
-                for (int b = tid; b < nb; b += kSampThreads) hist_m[b] = 0.0;
+                for (int b = tid; b < nb; b += kSampThreads) hist_u[b] = 0ull;
                 __syncthreads();
                 const unsigned long long hmask = shift + w >= 64 ? 0ULL : (~0ULL << (shift + w));
                 for (int i = tid; i < V; i += kSampThreads) {
                     const double v = q[i];
                     const unsigned long long bits = (unsigned long long)__double_as_longlong(v);
-                    if ((bits & hmask) == prefix) atomicAdd(&hist_m[(bits >> shift) & (nb - 1)], v);
+                    if ((bits & hmask) == prefix) atomicAdd(&hist_u[(bits >> shift) & (nb - 1)], __double2ull_rn(v * kFix));
                 }
                 __syncthreads();
                 if (tid == 0) {
-                    double cum = above;
+                    unsigned long long cum = above_u;
                     int sel = 0;
                     for (int b = nb - 1; b >= 0; b--) {
-                        if (cum + hist_m[b] >= a.top_p) { sel = b; break; }
-                        cum += hist_m[b];
+                        if (cum + hist_u[b] >= top_u) { sel = b; break; }
+                        cum += hist_u[b];
                     }
-                    s_r = cum;
+                    s_cum = cum;
                     s_sel = prefix | ((unsigned long long)sel << shift);
                 }
                 __syncthreads();
-                above = s_r;
+                above_u = s_cum;
                 prefix = s_sel;
                 __syncthreads();
             }
+            const double above = (double)above_u / kFix;
             cut = prefix;
             // ties at the cutoff value are taken in index order until the cumulative mass reaches top_p
             const double vc = __longlong_as_double((long long)cut);

@@ -255,7 +255,8 @@ int32_t qw_last_launch_count(const qw_model *m);
  * per row to argmax_out (batch) int32.  Stands in for rmsnorm(final) + dense(wcls) +
  * indexOfMax (Qwen3.java:402-405, AggregationFeatures.java:111-121,
  * AutoregressiveModel.java:412-420).  Its cross-CTA scratch is allocated with cudaMalloc on
- * the first call per device and kept for the life of the process. */
+ * the first call per device and kept for the life of the process; every call on a device shares
+ * it, so calls that overlap on the GPU (different streams, no ordering between them) race. */
 qw_status qw_op_lm_head_argmax(const void *w, int32_t w_dtype, int32_t vocab, int32_t dim, const float *x,
                                const float *norm_w, double eps, int32_t batch, float *logits_out,
                                int32_t *argmax_out, void *stream);

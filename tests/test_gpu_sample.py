@@ -121,3 +121,28 @@ def test_qwen3_api_temperature():
             want.append(O.sample_qwen3(lg, c["vocab"], 0.7, jr.next_double()))
     assert got == want[:10]
     o.close()
+
+
+def test_op_sample_nucleus_cutoff_at_mass_boundary_is_deterministic():
+    """top_p equal to the mass of the 50 largest probabilities (summed in sorted order, as sampleToken does): the
+    cutoff sits exactly on a boundary, where a rounding-order-dependent sum could keep one element more or less.
+    The device's mass sums are integer (fixed point), so 20 repeated draws give one answer, the reference's."""
+    import torch
+    rng = np.random.default_rng(77)
+    V = 151936
+    logits = (rng.standard_normal((1, V)) * 3).astype(np.float32)
+    p = np.exp(logits[0].astype(np.float64) - logits[0].max())
+    p /= p.sum()
+    top_p = float(np.sort(p)[::-1][:50].sum())
+    r = 0.9999  # the last kept element decides the draw
+    d_lg = torch.tensor(logits, device="cuda")
+    d_r = torch.tensor([r], dtype=torch.float64, device="cuda")
+    scratch = torch.empty(1, V, dtype=torch.float64, device="cuda")
+    got = set()
+    for _ in range(20):
+        out = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+        native.op_sample(d_lg.data_ptr(), 1, V, V, 1.0, top_p, 1, d_r.data_ptr(), scratch.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        got.add(int(out.item()))
+    assert len(got) == 1, got
+    assert got.pop() == O.sample_token(logits[0], V, 1.0, top_p, r)

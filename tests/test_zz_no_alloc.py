@@ -40,7 +40,10 @@ def test_static_scratch_matches_allocating_entry_point(dtype, batch, vocab, dim)
             assert int(got_a[b]) == int(np.argmax(lg[b]))
 
 
-def test_static_scratch_rejects_batch_beyond_limit():
+def test_static_scratch_entry_rejects_batch_outside_range():
+    """batch 5 is outside the op's [1, 4] rows: rejected with QW_ERR_SHAPE before any launch.  (The array's own
+    limit, SM count x 8 x batch <= 8192 partials, is out of reach on a 148-SM GPU: 148 x 8 x 4 = 4736.)"""
     with pytest.raises(native.QwenError) as e:
         native.op_lm_head_argmax_static(1, native.DTYPE_F32, 10, 64, 1, 1, 1e-6, 5, 0, 1)
     assert e.value.status == 2
+    assert "batch" in str(e.value)
