@@ -20,6 +20,7 @@
 #include "qw_prefill.h"
 #include "qw_ops.h"
 #include "qw_tc.h"
+#include "qw_ar.h"
 
 using namespace qw;
 
@@ -94,6 +95,10 @@ struct qw_model {
     unsigned *xch = nullptr;                // this rank's exchange buffer (tensor parallel step kernel)
     std::vector<void *> xch_peer;           // peers' exchange buffers opened through CUDA IPC
     unsigned **d_xch = nullptr;             // device array of all ranks' exchange buffers
+    unsigned long long *ar_buf = nullptr;   // this rank's all-reduce inboxes (batched decode under tensor parallelism)
+    unsigned long long **d_ar = nullptr;    // device array of all ranks' all-reduce inboxes
+    unsigned *ar_ctr = nullptr;             // generation | CTA arrivals of the all-reduce kernel
+    long long ar_cap = 0;                   // elements one all-reduce may carry
     unsigned *d_persist = nullptr;          // barrier generation + release word, persistent
     // sampling (qw_set_sampling): temperature <= 0 keeps greedy decoding
     double samp_temperature = 0.0, samp_top_p = 1.0;
@@ -363,6 +368,15 @@ int choose_flash_split(qw_model *m, int B) {
 }
 
 qw_status allreduce(qw_model *m, float *buf, size_t n) {
+    if (m->ar_buf && (long long)n <= m->ar_cap) {
+        // decode-sized: the two-shot flag-in-data kernel over NVLink (qw_allreduce.cu)
+        ArArgs a{};
+        a.x = buf; a.n = (long long)n; a.tp = m->tp; a.rank = m->rank; a.peers = m->d_ar;
+        a.gather_off = (long long)m->tp * (((long long)n + m->tp - 1) / m->tp);
+        a.gen = m->ar_ctr; a.done = m->ar_ctr + 1; a.err = m->pf.d_err;
+        LK(allreduce_ll_launch(a, m->num_sms, m->st));
+        return QW_OK;
+    }
     NK(ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, m->comm, m->st));
     return QW_OK;
 }
@@ -828,15 +842,16 @@ qw_status qw_get_unique_id(void *out128) {
     return QW_OK;
 }
 
-// Exchange buffers of the tensor-parallel step kernel: every rank allocates one, shares its CUDA IPC
-// handle through an NCCL all-gather and opens the others' (peer access over NVLink).
-static qw_status setup_exchange(qw_model *m) {
+// A device buffer of `bytes` on every rank that every peer opens through CUDA IPC (peer access over NVLink): the
+// handles travel through an NCCL all-gather.  *local is this rank's buffer, peer_maps the opened peer mappings (to
+// close), *d_ptrs a device array [tp] of every rank's pointer.
+static qw_status open_peer_buffer(qw_model *m, size_t bytes, void **local, std::vector<void *> &peer_maps,
+                                  void ***d_ptrs) {
     const int tp = m->tp;
-    const size_t words = 128 + (size_t)4 * tp * m->D;  // flags, sums, argmax, two [tp][D] inboxes of 8-byte words
-    CK(cudaMalloc((void **)&m->xch, words * sizeof(unsigned)));
-    CK(cudaMemset(m->xch, 0, words * sizeof(unsigned)));
+    CK(cudaMalloc(local, bytes));
+    CK(cudaMemset(*local, 0, bytes));
     cudaIpcMemHandle_t h;
-    CK(cudaIpcGetMemHandle(&h, m->xch));
+    CK(cudaIpcGetMemHandle(&h, *local));
     char *d_h = nullptr;
     CK(cudaMalloc((void **)&d_h, sizeof(h) * (tp + 1)));
     CK(cudaMemcpy(d_h + sizeof(h) * tp, &h, sizeof(h), cudaMemcpyHostToDevice));
@@ -847,17 +862,33 @@ static qw_status setup_exchange(qw_model *m) {
     cudaFree(d_h);
     if (nr != ncclSuccess) return fail(m, QW_ERR_NCCL, "exchange handles: %s", ncclGetErrorString(nr));
     if (e != cudaSuccess) return fail(m, QW_ERR_CUDA, "exchange handles: %s", cudaGetErrorString(e));
-    std::vector<unsigned *> ptrs(tp);
-    m->xch_peer.assign(tp, nullptr);
+    std::vector<void *> ptrs(tp);
     for (int p = 0; p < tp; p++) {
-        if (p == m->rank) { ptrs[p] = m->xch; continue; }
+        if (p == m->rank) { ptrs[p] = *local; continue; }
         void *q = nullptr;
         CK(cudaIpcOpenMemHandle(&q, all[p], cudaIpcMemLazyEnablePeerAccess));
-        m->xch_peer[p] = q;
-        ptrs[p] = (unsigned *)q;
+        peer_maps.push_back(q);
+        ptrs[p] = q;
     }
-    AL(m->d_xch, tp);
-    CK(cudaMemcpy(m->d_xch, ptrs.data(), sizeof(unsigned *) * tp, cudaMemcpyHostToDevice));
+    CK(cudaMalloc((void **)d_ptrs, sizeof(void *) * tp));
+    CK(cudaMemcpy(*d_ptrs, ptrs.data(), sizeof(void *) * tp, cudaMemcpyHostToDevice));
+    return QW_OK;
+}
+
+// Exchange buffers of the tensor-parallel step kernel: flags, sums, argmax, two [tp][D] inboxes of 8-byte words.
+static qw_status setup_exchange(qw_model *m) {
+    const size_t words = 128 + (size_t)4 * m->tp * m->D;
+    return open_peer_buffer(m, words * sizeof(unsigned), (void **)&m->xch, m->xch_peer, (void ***)&m->d_xch);
+}
+
+// Inboxes of the batched decode step's all-reduce (qw_allreduce.cu): up to max_batch x dim elements.
+static qw_status setup_allreduce(qw_model *m) {
+    m->ar_cap = (long long)m->B * m->D;
+    const size_t words = (size_t)allreduce_ll_words(m->ar_cap, m->tp);
+    qw_status s = open_peer_buffer(m, words * 8, (void **)&m->ar_buf, m->xch_peer, (void ***)&m->d_ar);
+    if (s) return s;
+    AL(m->ar_ctr, 2);
+    CK(cudaMemset(m->ar_ctr, 0, 2 * sizeof(unsigned)));
     return QW_OK;
 }
 
@@ -984,6 +1015,14 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
             if (m->tc_attn) CK(flash_prefill_tc_prepare());
         }
         AL(m->gu_split, (size_t)B * 2 * m->Fl);
+        if (tp_size > 1) {
+            // batched decode all-reduces over NVLink (QW_AR_NCCL=1: NCCL, for comparison)
+            const char *ev = getenv("QW_AR_NCCL");
+            if (!ev || atoi(ev) == 0) {
+                qw_status st = setup_allreduce(m);
+                if (st) return st;
+            }
+        }
     }
     // the persistent step kernel for batch-1 decode with bf16 weights at any tp (decode_kernels 0 or 2) when the
     // geometry fits it; under tensor parallelism its all-reduces are flag-in-data exchanges over NVLink
@@ -1528,6 +1567,7 @@ void qw_destroy(qw_model *m) {
     for (void *q : m->xch_peer)
         if (q) cudaIpcCloseMemHandle(q);
     cudaFree(m->xch); cudaFree(m->d_xch); cudaFree(m->d_persist);
+    cudaFree(m->ar_buf); cudaFree(m->d_ar); cudaFree(m->ar_ctr);
     cudaFree(m->d_rng); cudaFree(m->d_samp);
     if (m->h_pin_i) cudaFreeHost(m->h_pin_i);
     prefill_free(m->pf);
