@@ -101,6 +101,8 @@ struct FlashDecodeArgs {
     unsigned *counters;       // (B, Hkv), zero on entry, reset on exit
     __nv_bfloat16 *out;       // (B, ld_out)
     int ld_out;
+    int num_pages;            // pages of the KV pool (the TMA descriptors of the cache)
+    int *err;                 // device error word (bounded waits)
 };
 
 struct RowsArgmaxArgs {

@@ -599,7 +599,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             fd.slots = row_slot; fd.positions = row_pos; fd.H = m->Hl; fd.Hkv = m->Hkvl; fd.d = d;
             fd.nsplit = choose_flash_split(m, T); fd.scale = (float)(1.0 / sqrt((double)d));
             fd.part_o = m->part_o; fd.part_ml = m->part_ml; fd.counters = m->counters;
-            fd.out = pf.act; fd.ld_out = m->Ql;
+            fd.out = pf.act; fd.ld_out = m->Ql; fd.num_pages = m->num_pages; fd.err = pf.d_err;
             LKK(QW_KERNEL_ATTN, flash_decode_launch(fd, T, m->st));
         }
         // ---- O projection (+ residual) ----

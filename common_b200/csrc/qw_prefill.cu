@@ -13,6 +13,8 @@
 //   rows_argmax   first index of the maximum of each logits row (AggregationFeatures.java:111-121).
 #include "qw_internal.cuh"
 #include "qw_kernels.h"
+#include "qw_tc.h"
+#include "qw_tc_util.cuh"
 #include <float.h>
 #include <limits.h>
 
@@ -376,13 +378,23 @@ cudaError_t flash_prefill_launch(const FlashArgs &a, int nseq, cudaStream_t st) 
 // ------------------------------------------------------------------------------------------
 constexpr int kFdStages = 3;
 
+// byte offset of (row, 16-byte chunk) in a TMA-loaded [D / 64][64 rows][128 B] tile with the 128-byte swizzle
+__device__ __forceinline__ uint32_t fd_off(int row, int chunk) {
+    return (uint32_t)((chunk >> 3) * (kFaKeys * 128) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
 template <int D, int G>
-__global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDecodeArgs a) {
+__global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                         const __grid_constant__ CUtensorMap tmV,
+                                                                         FlashDecodeArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
     griddep_wait();               // the previous kernel's results
-    constexpr int CH = D / 8;
     constexpr int TILE_BYTES = kFaKeys * D * 2;
-    extern __shared__ __align__(128) uint8_t fsm[];
+    extern __shared__ __align__(128) uint8_t fsm_raw[];
+    // stages of [K tile | V tile], 1024-byte aligned for the swizzled TMA boxes
+    uint8_t *fsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(fsm_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t fd_full[kFdStages];
+    __shared__ int fd_abort;
     __shared__ float wm[kFaWarps][16], wl[kFaWarps][16];
     __shared__ float sw[G][kFaMaxSplit];
     __shared__ int s_last;
@@ -400,16 +412,30 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
     const __nv_bfloat16 *vc = reinterpret_cast<const __nv_bfloat16 *>(a.vcache);
     const int H = a.H, Hkv = a.Hkv;
 
+    if (tid == 0) {
+        for (int i = 0; i < kFdStages; i++) mbar_init(&fd_full[i], 1);
+        fd_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmK) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmV) : "memory");
+    }
+    __syncthreads();
+    volatile int *abort_flag = &fd_abort;
+    // K and V rows [kt * 64, kt * 64 + 64) of this KV head: boxes of min(page, 64) rows x 64 columns from the
+    // paged cache by TMA (one thread, no multicast); boxes past the last key read the zero fill
+    const int br = a.page_size < kFaKeys ? a.page_size : kFaKeys;
     auto load_tile = [&](int kt, int st) {
-        const uint32_t bk = smem_addr(fsm + st * 2 * TILE_BYTES), bv = bk + TILE_BYTES;
-        for (int i = tid; i < kFaKeys * CH; i += kFaWarps * 32) {
-            const int r = i / CH, c = i % CH;
+        if (tid != 0) return;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the stage are done
+        uint8_t *bk = fsm + st * 2 * TILE_BYTES, *bv = bk + TILE_BYTES;
+        mbar_arrive_expect_tx(&fd_full[st], 2 * TILE_BYTES);
+        for (int r = 0; r < kFaKeys; r += br) {
             const int p = kt * kFaKeys + r;
-            const bool ok = p < n;
-            const int page = ok ? ptab[p >> a.log2_page] : 0;
-            const size_t off = (((size_t)page * Hkv + kvh) * a.page_size + (p & (a.page_size - 1))) * D + c * 8;
-            cp_async16(bk + fa_off<D>(r, c), ok ? kc + off : kc, ok ? 16 : 0);
-            cp_async16(bv + fa_off<D>(r, c), ok ? vc + off : vc, ok ? 16 : 0);
+            const int y = p < n ? (ptab[p >> a.log2_page] * Hkv + kvh) * a.page_size + (p & (a.page_size - 1)) : -br;
+            for (int c = 0; c < D / 64; c++) {
+                tma_load_2d(bk + c * kFaKeys * 128 + r * 128, &tmK, &fd_full[st], c * 64, y);
+                tma_load_2d(bv + c * kFaKeys * 128 + r * 128, &tmV, &fd_full[st], c * 64, y);
+            }
         }
     };
 
@@ -420,11 +446,8 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
 
     if (kt0 < kt1) {
         // prologue: the first stages (the KV rows written by earlier kernels)
-#pragma unroll
-        for (int i = 0; i < kFdStages - 1; i++) {
+        for (int i = 0; i < kFdStages - 1; i++)
             if (kt0 + i < kt1) load_tile(kt0 + i, i);
-            cp_async_commit();
-        }
         // this warp's query rows: head kvh*G + row for row < G
         uint32_t qa[D / 16][4];
         {
@@ -442,9 +465,7 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
         for (int kt = kt0; kt < kt1; kt++) {
             const int st = (kt - kt0) % kFdStages;
             if (kt + kFdStages - 1 < kt1) load_tile(kt + kFdStages - 1, (kt - kt0 + kFdStages - 1) % kFdStages);
-            cp_async_commit();
-            cp_async_wait<kFdStages - 1>();
-            __syncthreads();
+            mbar_wait(&fd_full[st], (uint32_t)((kt - kt0) / kFdStages) & 1u, abort_flag, a.err);
             const uint32_t bk = smem_addr(fsm + st * 2 * TILE_BYTES), bv = bk + TILE_BYTES;
             float s[2][4];
             s[0][0] = s[0][1] = s[0][2] = s[0][3] = 0.f;
@@ -455,7 +476,7 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
                 const int key = warp * 16 + (i >> 1) * 8 + (lane & 7);
                 const int ch = kk * 2 + (i & 1);
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4(bk + fa_off<D>(key, ch), b0, b1, b2, b3);
+                ldsm_x4(bk + fd_off(key, ch), b0, b1, b2, b3);
                 mma_bf16(s[0], qa[kk], b0, b1);
                 mma_bf16(s[1], qa[kk], b2, b3);
             }
@@ -497,7 +518,7 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
                 const int key = warp * 16 + (i & 1) * 8 + (lane & 7);
                 const int ch = nj * 2 + (i >> 1);
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(bv + fa_off<D>(key, ch), b0, b1, b2, b3);
+                ldsm_x4_t(bv + fd_off(key, ch), b0, b1, b2, b3);
                 o[2 * nj][0] *= al_lo; o[2 * nj][1] *= al_lo; o[2 * nj][2] *= al_hi; o[2 * nj][3] *= al_hi;
                 o[2 * nj + 1][0] *= al_lo; o[2 * nj + 1][1] *= al_lo;
                 o[2 * nj + 1][2] *= al_hi; o[2 * nj + 1][3] *= al_hi;
@@ -506,7 +527,19 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
             }
             __syncthreads();  // stage st is refilled by a later iteration
         }
-        cp_async_wait<0>();
+        if (*abort_flag && tid == 0) {
+            // a wait gave up: let the copies still in flight land before the shared memory is released
+            const unsigned long long t0 = clock64();
+            for (int st = 0; st < kFdStages; st++) {
+                int last = -1;
+                for (int kt = kt0; kt < kt1; kt++)
+                    if ((kt - kt0) % kFdStages == st) last = kt;
+                if (last < 0) continue;
+                while (!mbar_try(smem_u32(&fd_full[st]), (uint32_t)((last - kt0) / kFdStages) & 1u) &&
+                       (unsigned long long)clock64() - t0 < kTcuWaitCycles) {
+                }
+            }
+        }
     }
 #pragma unroll
     for (int off = 1; off < 4; off <<= 1) l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
@@ -584,15 +617,22 @@ __global__ void __launch_bounds__(kFaWarps * 32) qw_flash_decode_kernel(FlashDec
 
 template <int D>
 static cudaError_t flash_decode_g(const FlashDecodeArgs &a, dim3 grid, cudaStream_t st) {
-    const size_t smem = (size_t)kFdStages * 2 * kFaKeys * D * 2;
+    const size_t smem = (size_t)kFdStages * 2 * kFaKeys * D * 2 + 1024;
     const dim3 block(kFaWarps * 32);
+    CUtensorMap mk, mv;
+    const long long rows = (long long)a.num_pages * a.Hkv * a.page_size;
+    const int br = a.page_size < kFaKeys ? a.page_size : kFaKeys;
+    cudaError_t e = tma_map_bf16_sw128(&mk, a.kcache, rows, D, D, br);
+    if (e != cudaSuccess) return e;
+    e = tma_map_bf16_sw128(&mv, a.vcache, rows, D, D, br);
+    if (e != cudaSuccess) return e;
     switch (a.H / a.Hkv) {
-        case 1: return launch_pdl(qw_flash_decode_kernel<D, 1>, grid, block, smem, st, a);
-        case 2: return launch_pdl(qw_flash_decode_kernel<D, 2>, grid, block, smem, st, a);
-        case 4: return launch_pdl(qw_flash_decode_kernel<D, 4>, grid, block, smem, st, a);
-        case 6: return launch_pdl(qw_flash_decode_kernel<D, 6>, grid, block, smem, st, a);
-        case 7: return launch_pdl(qw_flash_decode_kernel<D, 7>, grid, block, smem, st, a);
-        case 8: return launch_pdl(qw_flash_decode_kernel<D, 8>, grid, block, smem, st, a);
+        case 1: return launch_pdl(qw_flash_decode_kernel<D, 1>, grid, block, smem, st, mk, mv, a);
+        case 2: return launch_pdl(qw_flash_decode_kernel<D, 2>, grid, block, smem, st, mk, mv, a);
+        case 4: return launch_pdl(qw_flash_decode_kernel<D, 4>, grid, block, smem, st, mk, mv, a);
+        case 6: return launch_pdl(qw_flash_decode_kernel<D, 6>, grid, block, smem, st, mk, mv, a);
+        case 7: return launch_pdl(qw_flash_decode_kernel<D, 7>, grid, block, smem, st, mk, mv, a);
+        case 8: return launch_pdl(qw_flash_decode_kernel<D, 8>, grid, block, smem, st, mk, mv, a);
         default: return cudaErrorInvalidValue;
     }
 }
