@@ -28,6 +28,8 @@
 // lets its issued copies and MMAs land, frees its TMEM and returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <float.h>
+#include <limits.h>
 #include <mutex>
 
 #include "qw_internal.cuh"
@@ -66,6 +68,98 @@ __device__ __forceinline__ TileCoord tile_coord(int tile, int nf, int nt, int nk
     c.kb0 = (int)(((long long)nkb * c.ks) / nks);
     c.kb1 = (int)(((long long)nkb * (c.ks + 1)) / nks);
     return c;
+}
+
+// Epilogue of 32 consecutive tokens t0 .. t0+nj-1 of feature f (this lane) from the tile's sums v[j].
+// split: 0 = whole sums; 1 + ks = K range ks of an atomically accumulated split (bias with range 0 only).
+template <int EPI>
+__device__ __forceinline__ void tc_emit(const TcArgs &a, float (&v)[32], const TileCoord &c, int f, int q, int lane,
+                                        int t0, int nj, int split, uint8_t *sStage) {
+    if (EPI == TC_SWIGLU) {
+        // up * silu(gate) for this warp's 16 pairs x 32 tokens, staged as [token][64 pairs] bf16
+        // so that the 4 epilogue warps then write whole 128-byte rows
+        uint16_t *stg = reinterpret_cast<uint16_t *>(sStage);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float g = v[j];
+            const float u = __shfl_down_sync(0xffffffffu, g, 16);
+            if (lane < 16) {
+                const float h = u * __fdividef(g, 1.0f + __expf(-g));
+                stg[j * 64 + q * 16 + lane] = f2bf_bits(h);
+            }
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        {
+            const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
+            const int pair0 = c.f0 >> 1;
+            const int npair = min(64, (a.M - c.f0) >> 1);
+            __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(a.out);
+#pragma unroll
+            for (int k2 = 0; k2 < 2; k2++) {
+                const int idx = et + k2 * 128;  // 256 chunks of 16 bytes: 32 rows x 8
+                const int row = idx >> 3, ch = idx & 7;
+                if (row < nj && ch * 8 < npair) {
+                    const uint4 u = *reinterpret_cast<const uint4 *>(stg + row * 64 + ch * 8);
+                    *reinterpret_cast<uint4 *>(o + (size_t)(t0 + row) * a.ld_out + pair0 + ch * 8) = u;
+                }
+            }
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+    } else if (EPI == TC_ARGMAX) {
+        // logits (optional), then the first maximum of this warp's 32 features for each of the
+        // 32 tokens: a transposing butterfly leaves token j's winner in lane j
+        int id[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            if (f >= a.M) v[j] = -FLT_MAX;
+            id[j] = f < a.M ? f : INT_MAX;
+        }
+        if (a.out && f < a.M) {
+            float *o = reinterpret_cast<float *>(a.out);
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (j < nj) o[(size_t)(t0 + j) * a.ld_out + f] = v[j];
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < o; j++) {
+                const float sv = up ? v[j] : v[j + o], kv = up ? v[j + o] : v[j];
+                const int si = up ? id[j] : id[j + o], ki = up ? id[j + o] : id[j];
+                const float rv = __shfl_xor_sync(0xffffffffu, sv, o);
+                const int ri = __shfl_xor_sync(0xffffffffu, si, o);
+                const bool take = rv > kv || (rv == kv && ri < ki);
+                v[j] = take ? rv : kv;
+                id[j] = take ? ri : ki;
+            }
+        }
+        if (lane < nj) {
+            const size_t ci = (size_t)(t0 + lane) * a.ncand + (c.f0 >> 5) + q;
+            a.cand_val[ci] = v[0];
+            a.cand_idx[ci] = id[0];
+        }
+    } else if (f < a.M) {
+        float *o = reinterpret_cast<float *>(a.out);
+        const float bias = (a.bias && split <= 1) ? a.bias[f] : 0.f;
+        if (split) {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (j < nj) atomicAdd(o + (size_t)(t0 + j) * a.ld_out + f, v[j] + bias);
+        } else if (EPI == TC_RESID) {
+            // all residual loads first (out may alias resid), then the stores
+            float rv[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) rv[j] = j < nj ? a.resid[(size_t)(t0 + j) * a.ld_resid + f] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (j < nj) o[(size_t)(t0 + j) * a.ld_out + f] = rv[j] + v[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (j < nj) o[(size_t)(t0 + j) * a.ld_out + f] = v[j] + bias;
+        }
+    }
 }
 
 template <int BN, int EPI>
@@ -216,58 +310,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint32_t r[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + cc), r);
                 const int nj = min(32, ncols - cc);
-                if (EPI == TC_SWIGLU) {
-                    // up * silu(gate) for this warp's 16 pairs x 32 tokens, staged as [token][64 pairs] bf16
-                    // so that the 4 epilogue warps then write whole 128-byte rows
-                    uint16_t *stg = reinterpret_cast<uint16_t *>(sStage);
+                float v[32];
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const float g = __uint_as_float(r[j]);
-                        const float u = __shfl_down_sync(0xffffffffu, g, 16);
-                        if (lane < 16) {
-                            const float h = u * __fdividef(g, 1.0f + __expf(-g));
-                            stg[j * 64 + q * 16 + lane] = f2bf_bits(h);
-                        }
-                    }
-                    asm volatile("bar.sync 2, 128;" ::: "memory");
-                    {
-                        const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
-                        const int pair0 = c.f0 >> 1;
-                        const int npair = min(64, (a.M - c.f0) >> 1);
-                        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(a.out);
-#pragma unroll
-                        for (int k2 = 0; k2 < 2; k2++) {
-                            const int idx = et + k2 * 128;  // 256 chunks of 16 bytes: 32 rows x 8
-                            const int row = idx >> 3, ch = idx & 7;
-                            if (row < nj && ch * 8 < npair) {
-                                const uint4 v = *reinterpret_cast<const uint4 *>(stg + row * 64 + ch * 8);
-                                *reinterpret_cast<uint4 *>(o + (size_t)(tbase + cc + row) * a.ld_out + pair0 + ch * 8) = v;
-                            }
-                        }
-                    }
-                    asm volatile("bar.sync 2, 128;" ::: "memory");
-                } else if (f < a.M) {
-                    float *o = reinterpret_cast<float *>(a.out);
-                    const float bias = (a.bias && c.ks == 0) ? a.bias[f] : 0.f;
-                    if (nks > 1) {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (j < nj) atomicAdd(o + (size_t)(tbase + cc + j) * a.ld_out + f, __uint_as_float(r[j]) + bias);
-                    } else if (EPI == TC_RESID) {
-                        // all residual loads first (out may alias resid), then the stores
-                        float rv[32];
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            rv[j] = j < nj ? a.resid[(size_t)(tbase + cc + j) * a.ld_resid + f] : 0.f;
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (j < nj) o[(size_t)(tbase + cc + j) * a.ld_out + f] = rv[j] + __uint_as_float(r[j]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (j < nj) o[(size_t)(tbase + cc + j) * a.ld_out + f] = __uint_as_float(r[j]) + bias;
-                    }
-                }
+                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                tc_emit<EPI>(a, v, c, f, q, lane, tbase + cc, nj, nks > 1 ? 1 + c.ks : 0, sStage);
             }
             tc_fence_before();
             __syncwarp();
@@ -345,18 +391,24 @@ cudaError_t tma_map_bf16_sw128(CUtensorMap *m, const void *base, long long rows,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t tc_prepare() {
-    const void *fns[] = {(const void *)qw_tc_gemm_kernel<64, TC_STORE>,  (const void *)qw_tc_gemm_kernel<128, TC_STORE>,
-                         (const void *)qw_tc_gemm_kernel<256, TC_STORE>, (const void *)qw_tc_gemm_kernel<64, TC_RESID>,
-                         (const void *)qw_tc_gemm_kernel<128, TC_RESID>, (const void *)qw_tc_gemm_kernel<256, TC_RESID>,
-                         (const void *)qw_tc_gemm_kernel<64, TC_SWIGLU>, (const void *)qw_tc_gemm_kernel<128, TC_SWIGLU>,
-                         (const void *)qw_tc_gemm_kernel<256, TC_SWIGLU>};
-    const int bns[] = {64, 128, 256, 64, 128, 256, 64, 128, 256};
-    for (int i = 0; i < 9; i++) {
+template <int EPI>
+static cudaError_t prepare_epi() {
+    const void *fns[] = {(const void *)qw_tc_gemm_kernel<64, EPI>, (const void *)qw_tc_gemm_kernel<128, EPI>,
+                         (const void *)qw_tc_gemm_kernel<256, EPI>};
+    const int bns[] = {64, 128, 256};
+    for (int i = 0; i < 3; i++) {
         cudaError_t e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes(bns[i]));
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+cudaError_t tc_prepare() {
+    cudaError_t e = prepare_epi<TC_STORE>();
+    if (e == cudaSuccess) e = prepare_epi<TC_RESID>();
+    if (e == cudaSuccess) e = prepare_epi<TC_SWIGLU>();
+    if (e == cudaSuccess) e = prepare_epi<TC_ARGMAX>();
+    return e;
 }
 
 int tc_pick_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
@@ -384,6 +436,8 @@ cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int ep
     if (a.M < 1 || a.T < 1 || a.K < 8 || a.K % 8 || a.ksplit < 1) return cudaErrorInvalidValue;
     if (a.ksplit > (a.K + kBK - 1) / kBK) return cudaErrorInvalidValue;
     if (epi == TC_SWIGLU && (a.ksplit != 1 || a.M % 32)) return cudaErrorInvalidValue;
+    if (epi == TC_ARGMAX && (a.ksplit != 1 || !a.cand_val || !a.cand_idx || a.ncand < (a.M + kBM - 1) / kBM * 4))
+        return cudaErrorInvalidValue;
     if (epi == TC_RESID && a.ksplit > 1 && a.out != (const void *)a.resid) return cudaErrorInvalidValue;
     if (bn == 0) bn = tc_pick_bn(a.T);
     CUtensorMap mw, mx;
@@ -395,6 +449,7 @@ cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int ep
         case TC_STORE: return launch_epi<TC_STORE>(mw, mx, a, bn, num_sms, st);
         case TC_RESID: return launch_epi<TC_RESID>(mw, mx, a, bn, num_sms, st);
         case TC_SWIGLU: return launch_epi<TC_SWIGLU>(mw, mx, a, bn, num_sms, st);
+        case TC_ARGMAX: return launch_epi<TC_ARGMAX>(mw, mx, a, bn, num_sms, st);
     }
     return cudaErrorInvalidValue;
 }

@@ -38,13 +38,14 @@ cudaError_t qk_sumsq_launch(const float *qkv, int ld, int qw, int kw, int B, flo
 cudaError_t hold_launch(unsigned long long ns, cudaStream_t st);
 cudaError_t add_launch(float *out, const float *a, const float *b, size_t n, cudaStream_t st);
 cudaError_t zero_launch(float *out, size_t n, cudaStream_t st);  // programmatically launched; memset when unaligned
-cudaError_t swiglu_rows_launch(const float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st);
+cudaError_t swiglu_rows_launch(float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st);  // zeroes gu after reading
 
 struct NormRowsArgs {
     float *x;  // (rows, ld_x) fp32 residual stream: read, or written when embed / part is given
     int ld_x;
-    const float *part;  // optional (rows, ld_part) all-reduced partial added to x (and stored)
+    float *part;  // optional (rows, ld_part) all-reduced partial added to x (and stored)
     int ld_part;
+    int zero_part;  // write zeros over the partial after reading it (the next split-K GEMM accumulates into it)
     const __nv_bfloat16 *embed;  // optional (vocab, K) bf16 table: x = embed[tokens[r]] (stored)
     const int *tokens;
     const float *w;  // rmsnorm weight (K)
@@ -55,8 +56,9 @@ struct NormRowsArgs {
 };
 
 struct QkvPostArgs {
-    const float *qkv;  // (rows, ld_qkv) fp32: q | k | v of this rank's heads
+    float *qkv;  // (rows, ld_qkv) fp32: q | k | v of this rank's heads
     int ld_qkv;
+    int zero_qkv;  // write zeros over the rows read (the next split-K GEMM accumulates into them)
     const float *qn, *kn;
     int qk_mode;         // 0 none, 1 whole vector, 2 per head
     const float *qk_ss;  // optional (rows, 2) global sums of squares (vector mode, tp > 1)
@@ -108,6 +110,8 @@ struct FlashDecodeArgs {
 struct RowsArgmaxArgs {
     const float *logits;  // (rows, ld)
     int ld, n;
+    const float *cand_val;  // instead of logits: (rows, ld) candidate maxima with their indices (n per row)
+    const int *cand_idx;
     int idx_offset;
     int *argmax_out;
     float *argmax_val;

@@ -148,22 +148,29 @@ cudaError_t zero_launch(float *out, size_t n, cudaStream_t st) {
     return launch_pdl(qw_zero_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<float4 *>(out), n / 4);
 }
 
-// h[t][p] = up * silu(gate) for rows of the (2F) gate/up projection interleaved in blocks of 16 gate then 16 up
+// h[t][p] = up * silu(gate), then gu = 0, for rows of the (2F) gate/up projection interleaved in blocks of 16 gate then 16 up
 // rows, as the GEMM's SwiGLU epilogue computes it (same expression), h bf16 (T, F).
-__global__ void qw_swiglu_rows_kernel(const float *gu, int F, __nv_bfloat16 *h) {
+__global__ void qw_swiglu_rows_kernel(float *gu, int F, __nv_bfloat16 *h) {
     griddep_launch_dependents();
     griddep_wait();
     const int t = blockIdx.y;
-    const float *row = gu + (size_t)t * 2 * F;
-    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < F; p += gridDim.x * blockDim.x) {
-        const int b = p / kGuBlock, j = p % kGuBlock;
-        const float g = row[b * 2 * kGuBlock + j], u = row[b * 2 * kGuBlock + kGuBlock + j];
-        h[(size_t)t * F + p] = __float2bfloat16(u * __fdividef(g, 1.0f + __expf(-g)));
-    }
+    float *row = gu + (size_t)t * 2 * F;
+    const int p = (blockIdx.x * blockDim.x + threadIdx.x) * 4;  // four pairs of one 16-row block
+    if (p >= F) return;
+    float4 *pg = reinterpret_cast<float4 *>(row + (p / kGuBlock) * 2 * kGuBlock + p % kGuBlock);
+    const float4 g = pg[0], u = pg[kGuBlock / 4];
+    pg[0] = make_float4(0.f, 0.f, 0.f, 0.f);  // zeroed again for the next split-K accumulation into this buffer
+    pg[kGuBlock / 4] = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint2 o;
+    o.x = (uint32_t)f2bf_bits(u.x * __fdividef(g.x, 1.0f + __expf(-g.x))) |
+          ((uint32_t)f2bf_bits(u.y * __fdividef(g.y, 1.0f + __expf(-g.y))) << 16);
+    o.y = (uint32_t)f2bf_bits(u.z * __fdividef(g.z, 1.0f + __expf(-g.z))) |
+          ((uint32_t)f2bf_bits(u.w * __fdividef(g.w, 1.0f + __expf(-g.w))) << 16);
+    *reinterpret_cast<uint2 *>(h + (size_t)t * F + p) = o;
 }
-cudaError_t swiglu_rows_launch(const float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st) {
-    if (T < 1 || F < 1) return cudaErrorInvalidValue;
-    const int bx = (F + 255) / 256 < 8 ? (F + 255) / 256 : 8;
+cudaError_t swiglu_rows_launch(float *gu, int T, int F, __nv_bfloat16 *h, cudaStream_t st) {
+    if (T < 1 || F < 1 || F % kGuBlock) return cudaErrorInvalidValue;
+    const int bx = (F / 4 + 255) / 256;
     return launch_pdl(qw_swiglu_rows_kernel, dim3(bx, T), dim3(256), 0, st, gu, F, h);
 }
 

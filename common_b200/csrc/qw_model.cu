@@ -91,6 +91,11 @@ struct qw_model {
     size_t step_zero_words = 0;
     float *gu = nullptr;
     float *gu_split = nullptr;  // (max_batch, 2 Fl) fp32: gate/up of a split-K batched decode projection
+    float *qkv_split = nullptr; // (max_batch, QKVl) fp32: QKV of a split-K batched decode projection
+    float *part_split = nullptr; // (max_batch, D) fp32: O / down partial of a split-K tensor-parallel decode
+    // (both accumulate with atomics and are zeroed again by the kernel that reads them, so no zeroing launch)
+    float *cand_val = nullptr;  // (max_batch, 4 x lm_head tiles) argmax candidates of the batched lm_head
+    int *cand_idx = nullptr;
     unsigned long long *d_trace = nullptr;  // per-phase timestamps of a profiled step
     unsigned *xch = nullptr;                // this rank's exchange buffer (tensor parallel step kernel)
     std::vector<void *> xch_peer;           // peers' exchange buffers opened through CUDA IPC
@@ -531,7 +536,7 @@ qw_status tc_gemm(qw_model *m, int kind, const void *W, const void *X, int M, in
     a.M = M; a.T = T; a.K = K;
     a.ksplit = allow_split ? tc_pick_ksplit(M, T, K, bn, m->num_sms) : 1;
     a.out = out; a.ld_out = ld_out; a.resid = resid; a.ld_resid = ld_out; a.bias = bias; a.err = m->pf.d_err;
-    if (a.ksplit > 1 && epi == TC_STORE) CK(zero_launch((float *)out, (size_t)T * ld_out, m->st));
+    // a split STORE accumulates with atomics into a buffer its consumer keeps zeroed (qkv_split, gu_split)
     LKK(kind, tc_gemm_launch(W, X, a, epi, bn, m->num_sms, m->st));
     return QW_OK;
 }
@@ -559,16 +564,20 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         Layer &Ly = m->L[l];
         // ---- residual update + rmsnorm -> bf16 rows ----
         NormRowsArgs na{};
-        na.x = x; na.ld_x = D; na.part = pending; na.ld_part = D;
+        na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
         if (l == 0 && !x_in) { na.embed = (const __nv_bfloat16 *)m->embed; na.tokens = tokens; }
         na.w = Ly.rms_att; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
         LK(norm_rows_launch(na, T, m->st));
         pending = nullptr;
         // ---- fused QKV projection ----
-        TRY(tc_gemm(m, QW_KERNEL_QKV, Ly.w_qkv, pf.act, m->QKVl, T, D, TC_STORE, m->qkv, m->QKVl, nullptr, Ly.b_qkv, true));
+        // split K (skinny decode shapes): atomics into qkv_split, which qkv_post zeroes again after reading it
+        const bool qkv_sp = T <= m->B && tc_pick_ksplit(m->QKVl, T, D, tc_pick_bn(T), m->num_sms) > 1;
+        float *qkv = qkv_sp ? m->qkv_split : m->qkv;
+        TRY(tc_gemm(m, QW_KERNEL_QKV, Ly.w_qkv, pf.act, m->QKVl, T, D, TC_STORE, qkv, m->QKVl, nullptr, Ly.b_qkv,
+                    qkv_sp));
         const float *qk_ss = nullptr;
         if (tpm && c.qk_norm == QW_QKNORM_VECTOR) {
-            LK(qk_sumsq_launch(m->qkv, m->QKVl, m->Ql, m->KVl, T, pf.row_ss, m->st));
+            LK(qk_sumsq_launch(qkv, m->QKVl, m->Ql, m->KVl, T, pf.row_ss, m->st));
             TRY(allreduce(m, pf.row_ss, (size_t)T * 2));
             qk_ss = pf.row_ss;
         }
@@ -576,7 +585,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         void *vc = (char *)m->vpool + (size_t)l * m->layer_kv_elems * m->kvsz;
         {
             QkvPostArgs qa{};
-            qa.qkv = m->qkv; qa.ld_qkv = m->QKVl; qa.qn = Ly.qn; qa.kn = Ly.kn; qa.qk_mode = c.qk_norm; qa.qk_ss = qk_ss;
+            qa.qkv = qkv; qa.zero_qkv = qkv_sp; qa.ld_qkv = m->QKVl; qa.qn = Ly.qn; qa.kn = Ly.kn; qa.qk_mode = c.qk_norm; qa.qk_ss = qk_ss;
             qa.q_total = c.heads * d; qa.kv_total = c.kv_heads * d; qa.freq = m->freq;
             qa.slots = row_slot; qa.positions = row_pos; qa.page_table = m->d_page_table; qa.max_pages = m->max_pages;
             qa.page_size = m->page_size; qa.log2_page = m->log2_page; qa.kcache = kc; qa.vcache = vc;
@@ -604,15 +613,18 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         }
         // ---- O projection (+ residual) ----
         if (tpm) {
-            TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, m->part, D, nullptr, nullptr, true));
-            TRY(allreduce(m, m->part, (size_t)T * D));
-            pending = m->part;
+            // decode: split K with atomics into part_split, which the next rmsnorm zeroes again after reading it
+            const bool sp = !prefill && T <= m->B;
+            float *pb = sp ? m->part_split : m->part;
+            TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, pb, D, nullptr, nullptr, sp));
+            TRY(allreduce(m, pb, (size_t)T * D));
+            pending = pb;
         } else {
             TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_RESID, x, D, x, nullptr, true));
         }
         // ---- residual update + rmsnorm ----
         na = NormRowsArgs{};
-        na.x = x; na.ld_x = D; na.part = pending; na.ld_part = D;
+        na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
         na.w = Ly.rms_ffn; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
         LK(norm_rows_launch(na, T, m->st));
         pending = nullptr;
@@ -628,9 +640,12 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
                         false));
         }
         if (tpm) {
-            TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, m->part, D, nullptr, nullptr, true));
-            TRY(allreduce(m, m->part, (size_t)T * D));
-            pending = m->part;
+            // decode: split K with atomics into part_split, which the next rmsnorm zeroes again after reading it
+            const bool sp = !prefill && T <= m->B;
+            float *pb = sp ? m->part_split : m->part;
+            TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, pb, D, nullptr, nullptr, sp));
+            TRY(allreduce(m, pb, (size_t)T * D));
+            pending = pb;
         } else {
             TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_RESID, x, D, x, nullptr, true));
         }
@@ -646,13 +661,21 @@ qw_status tc_decode(qw_model *m, int *tokens, const float *x_in, const int *slot
     TRY(tc_layers(m, B, tokens, x_in, slots, positions, false, 0, 0, 1, nullptr, &pending));
     const bool tpm = m->tp > 1;
     NormRowsArgs na{};
-    na.x = m->xa; na.ld_x = m->D; na.part = pending; na.ld_part = m->D;
+    na.x = m->xa; na.ld_x = m->D; na.part = const_cast<float *>(pending); na.ld_part = m->D; na.zero_part = pending == m->part_split;
     na.w = m->norm_final; na.eps = (float)m->c.eps; na.out = m->pf.act; na.ld_out = m->D; na.K = m->D;
     LK(norm_rows_launch(na, B, m->st));
-    float *lg = (!tpm && logits_out_dev) ? logits_out_dev : m->logits;
-    TRY(tc_gemm(m, QW_KERNEL_LM_HEAD, m->lm, m->pf.act, m->Vl, B, m->D, TC_STORE, lg, m->Vl, nullptr, nullptr, false));
+    // lm_head with the argmax candidates of every 32 vocabulary rows in its epilogue; logits only when asked for
+    float *lg = logits_out_dev ? (tpm ? m->logits : logits_out_dev) : nullptr;
+    const int ncand = (m->Vl + 127) / 128 * 4;
+    {
+        TcArgs a{};
+        a.M = m->Vl; a.T = B; a.K = m->D; a.ksplit = 1;
+        a.out = lg; a.ld_out = m->Vl; a.err = m->pf.d_err;
+        a.cand_val = m->cand_val; a.cand_idx = m->cand_idx; a.ncand = ncand;
+        LKK(QW_KERNEL_LM_HEAD, tc_gemm_launch(m->lm, m->pf.act, a, TC_ARGMAX, tc_pick_bn(B), m->num_sms, m->st));
+    }
     RowsArgmaxArgs ra{};
-    ra.logits = lg; ra.ld = m->Vl; ra.n = m->Vl; ra.idx_offset = m->v0;
+    ra.cand_val = m->cand_val; ra.cand_idx = m->cand_idx; ra.ld = ncand; ra.n = ncand; ra.idx_offset = m->v0;
     if (!tpm) {
         ra.argmax_out = argmax_dev; ra.next_tokens = tokens; ra.positions = positions; ra.advance = advance;
         ra.hist = hist; ra.hist_ld = hist_ld;
@@ -1015,6 +1038,13 @@ static qw_status create_impl(qw_model *m, const qw_config *cfg, int device, int 
             if (m->tc_attn) CK(flash_prefill_tc_prepare());
         }
         AL(m->gu_split, (size_t)B * 2 * m->Fl);
+        AL(m->qkv_split, (size_t)B * m->QKVl);
+        AL(m->part_split, (size_t)B * m->D);
+        CK(cudaMemset(m->part_split, 0, sizeof(float) * (size_t)B * m->D));
+        CK(cudaMemset(m->gu_split, 0, sizeof(float) * (size_t)B * 2 * m->Fl));
+        CK(cudaMemset(m->qkv_split, 0, sizeof(float) * (size_t)B * m->QKVl));
+        AL(m->cand_val, (size_t)B * ((m->Vl + 127) / 128 * 4));
+        AL(m->cand_idx, (size_t)B * ((m->Vl + 127) / 128 * 4));
         if (tp_size > 1) {
             // batched decode all-reduces over NVLink (QW_AR_NCCL=1: NCCL, for comparison)
             const char *ev = getenv("QW_AR_NCCL");
@@ -1563,7 +1593,7 @@ void qw_destroy(qw_model *m) {
     cudaFree(m->part_o); cudaFree(m->part_ml); cudaFree(m->qk_ss); cudaFree(m->counters); cudaFree(m->am_counter);
     cudaFree(m->am_pval); cudaFree(m->am_pidx); cudaFree(m->am_val); cudaFree(m->am_idx); cudaFree(m->am_val_all);
     cudaFree(m->am_idx_all); cudaFree(m->logits); cudaFree(m->logits_all); cudaFree(m->d_tokens); cudaFree(m->d_argmax);
-    cudaFree(m->d_step_layers); cudaFree(m->d_bar); cudaFree(m->gu); cudaFree(m->gu_split); cudaFree(m->d_trace);
+    cudaFree(m->d_step_layers); cudaFree(m->d_bar); cudaFree(m->gu); cudaFree(m->gu_split); cudaFree(m->qkv_split); cudaFree(m->part_split); cudaFree(m->cand_val); cudaFree(m->cand_idx); cudaFree(m->d_trace);
     for (void *q : m->xch_peer)
         if (q) cudaIpcCloseMemHandle(q);
     cudaFree(m->xch); cudaFree(m->d_xch); cudaFree(m->d_persist);

@@ -23,7 +23,7 @@ namespace qw {
 // ------------------------------------------------------------------------------------------
 // norm_rows: one CTA per token row
 // ------------------------------------------------------------------------------------------
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 512;
 constexpr size_t kPrepSmem = 160 * 1024;  // dynamic shared memory the row kernels are opted in to
 
 __global__ void __launch_bounds__(kNormThreads) qw_norm_rows_kernel(NormRowsArgs a) {
@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(kNormThreads) qw_norm_rows_kernel(NormRowsArgs
         }
         if (a.part) {
             float4 p = *reinterpret_cast<const float4 *>(a.part + (size_t)r * a.ld_part + k);
+            if (a.zero_part) *reinterpret_cast<float4 *>(a.part + (size_t)r * a.ld_part + k) = make_float4(0.f, 0.f, 0.f, 0.f);
             v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
         }
         if (erow || a.part) *reinterpret_cast<float4 *>(a.x + (size_t)r * a.ld_x + k) = v;
@@ -77,7 +78,7 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
 // ------------------------------------------------------------------------------------------
 // qkv_post: one CTA per token row
 // ------------------------------------------------------------------------------------------
-constexpr int kPostThreads = 256;
+constexpr int kPostThreads = 512;
 
 template <typename KT>
 __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a) {
@@ -95,6 +96,12 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
         row[i] = v;
         if (i < Ql) sq += v * v;
         else if (i < Ql + KVl) sk += v * v;
+    }
+    if (a.zero_qkv) {
+        // zeroed again for the next split-K accumulation into this buffer (after all loads of the row)
+        __syncthreads();
+        for (int i = tid * 4; i < W; i += kPostThreads * 4)
+            *reinterpret_cast<float4 *>(a.qkv + (size_t)r * a.ld_qkv + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (a.qk_mode == 1) {
         sq = warp_sum(sq);
@@ -657,9 +664,19 @@ __global__ void __launch_bounds__(512) qw_rows_argmax_kernel(RowsArgmaxArgs a) {
     const float *row = a.logits + (size_t)b * a.ld;
     float bv = -FLT_MAX;
     int bi = INT_MAX;
-    for (int i = tid; i < a.n; i += blockDim.x) {
-        const float v = row[i];
-        if (v > bv) { bv = v; bi = i; }  // increasing i per thread: strict > keeps the first
+    if (a.cand_val) {
+        const float *cv = a.cand_val + (size_t)b * a.ld;
+        const int *ci = a.cand_idx + (size_t)b * a.ld;
+        for (int i = tid; i < a.n; i += blockDim.x) {
+            const float v = cv[i];
+            const int ix = ci[i];
+            if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
+        }
+    } else {
+        for (int i = tid; i < a.n; i += blockDim.x) {
+            const float v = row[i];
+            if (v > bv) { bv = v; bi = i; }  // increasing i per thread: strict > keeps the first
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

@@ -16,6 +16,8 @@ enum TcEpi {
     TC_STORE = 0,   // out_f32[t * ld_out + f] = acc (+ bias[f])
     TC_RESID = 1,   // out_f32[t * ld_out + f] = resid[t * ld_resid + f] + acc
     TC_SWIGLU = 2,  // W rows interleaved 16 gate / 16 up: out_bf16[t * ld_out + pair] = up * silu(gate)
+    TC_ARGMAX = 3,  // optional STORE (out may be null) and, per token and 32 features, the first maximum:
+                    // cand_val / cand_idx[t * ncand + f / 32] (ncand >= 4 x 128-row tiles of M)
 };
 
 // device-side error codes written to TcArgs::err
@@ -32,6 +34,9 @@ struct TcArgs {
     int ld_resid;
     const float *bias;  // STORE: optional (M)
     int *err;           // optional: set to TC_DEVERR_* when a bounded wait gives up
+    float *cand_val;    // ARGMAX: (T, ncand) per-group maxima and their feature indices
+    int *cand_idx;
+    int ncand;
 };
 
 // Build the TMA descriptors and launch.  bn = 0 picks the token tile from T.
