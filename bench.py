@@ -201,7 +201,12 @@ def run_batched(args, rank, world, local, nid, peaks):
     prefill = {"tok_s": NSEQ * L / (pms * 1e-3), "ms": pms, "seqs": NSEQ, "seq_len": L, "flops": fl,
                "tflops": tf, "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peak_tf, "unit": "TFLOP/s",
                                           "frac": tf / world / peak_tf, "per": "GPU",
-                                          "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback"},
+                                          "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback",
+                                          # the prefill runs for about half a second under the 1 kW power cap: the
+                                          # seconds-long cuBLAS loop is the like-for-like denominator
+                                          "peak_sustained": peaks.get("bf16_tflops_sustained"),
+                                          "frac_sustained": (tf / world / peaks["bf16_tflops_sustained"]
+                                                             if peaks.get("bf16_tflops_sustained") else None)},
                "flops_split": {"linear": lin, "attention_causal": att, "lm_head": "last position only"},
                "timing": "qw_prefill through the host API (tokens from host memory), CUDA events, best of "
                          f"{args.prefill_reps}" if world == 1 else "max over ranks"}

@@ -31,6 +31,7 @@
 #include <float.h>
 #include <limits.h>
 #include <mutex>
+#include <stdlib.h>
 
 #include "qw_internal.cuh"
 #include "qw_tc.h"
@@ -330,6 +331,213 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// CTA-pair variant for prefill shapes (cta_group::2): a cluster of two CTAs on two SMs computes a
+// 256-feature x 256-token tile with one tcgen05.mma stream (M = 256, N = 256) issued by the even CTA.
+// Each CTA stages its own 128 rows of W and its own 128 tokens of X per k-block (32 KB, six or seven stages),
+// so a stage carries half the X bytes of the one-CTA 128 x 256 tile and the ring is deeper, and each
+// CTA's TMEM holds the sums of its 128 features for all 256 tokens.
+//   full[s]   in the even CTA: one arrival (its producer's expect_tx of both CTAs' bytes); both CTAs'
+//             TMA loads count their bytes on it (cta_group::2 form, no multicast);
+//   empty[s]  in each CTA, signalled by the MMA commit to both CTAs of the pair;
+//   tfull[i]  in each CTA, signalled by the commit after the tile's last k-block;
+//   tempty[i] in the even CTA: 8 arrivals (the epilogue warps of both CTAs).
+// ---------------------------------------------------------------------------------------------
+constexpr int kPairBM = 256, kPairBN = 256, kPairHalfN = 128;
+constexpr int kPairStageBytes = (kBM + kPairHalfN) * kBK * 2;
+// seven stages (224 KB) where the epilogue stages nothing in shared memory, six beside SWIGLU's 4 KB rows
+__host__ __device__ constexpr int pair_stages(int epi) { return epi == TC_SWIGLU ? 6 : 7; }
+__host__ __device__ constexpr int pair_smem(int epi) {
+    return pair_stages(epi) * kPairStageBytes + 1024 + (epi == TC_SWIGLU ? 4096 : 0);
+}
+
+__device__ __forceinline__ TileCoord pair_tile_coord(int tile, int nf, int nt) {
+    TileCoord c;
+    const int per_group = nf * kGroupT;
+    const int g = tile / per_group, r = tile % per_group;
+    const int t_in = min(kGroupT, nt - g * kGroupT);
+    c.t0 = g * kGroupT + r % t_in;
+    c.f0 = (r / t_in) * kPairBM;
+    c.ks = 0;
+    c.kb0 = 0;
+    c.kb1 = 0;
+    return c;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    qw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                           const TcArgs a) {
+    constexpr int S = pair_stages(EPI);
+    constexpr int A_BYTES = kBM * kBK * 2, B_BYTES = kPairHalfN * kBK * 2;
+    constexpr uint32_t TMEM_COLS = 2 * kPairBN;
+    constexpr uint32_t IDESC = tc_idesc_f16(kPairBM, kPairBN);
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S], tfull_bar[2], tempty_bar[2], done_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * A_BYTES;
+    uint8_t *sStage = smem + S * (A_BYTES + B_BYTES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    volatile int *abort_flag = &abort_sh;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tfull_bar[i], 1);
+            mbar_init(&tempty_bar[i], 8);
+        }
+        mbar_init(&done_bar, 1);
+        abort_sh = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmW) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmX) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrival
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    griddep_launch_dependents();
+
+    const int nf = (a.M + kPairBM - 1) / kPairBM, nt = (a.T + kPairBN - 1) / kPairBN;
+    const int nkb = (a.K + kBK - 1) / kBK;
+    const int total = nf * nt;
+    const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            const uint32_t full0 = cluster_map(smem_u32(&full_bar[0]), 0);
+            int s = 0;
+            uint32_t ph = 0, issued = 0, last_ph = 0;
+            bool ok = true, waited = false;
+            int npend = 0, pend_kb[S], pend_t[S];
+            auto flush = [&]() {
+                griddep_wait();
+                waited = true;
+                for (int i = 0; i < npend; i++)
+                    tma_load_2d_pair(sB + i * B_BYTES, &tmX, full0 + 8u * i, pend_kb[i] * kBK, pend_t[i]);
+            };
+            for (int tile = cid; tile < total && ok; tile += ncl) {
+                const TileCoord c = pair_tile_coord(tile, nf, nt);
+                const int wrow = c.f0 + (int)rank * kBM, trow = c.t0 * kPairBN + (int)rank * kPairHalfN;
+                for (int kb = 0; kb < nkb; kb++) {
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, a.err)) { ok = false; break; }
+                    if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * (A_BYTES + B_BYTES));
+                    tma_load_2d_pair(sA + s * A_BYTES, &tmW, full0 + 8u * s, kb * kBK, wrow);
+                    if (waited) {
+                        tma_load_2d_pair(sB + s * B_BYTES, &tmX, full0 + 8u * s, kb * kBK, trow);
+                    } else {
+                        pend_kb[npend] = kb;
+                        pend_t[npend] = trow;
+                        if (++npend == S) flush();
+                    }
+                    issued |= 1u << s;
+                    last_ph = (last_ph & ~(1u << s)) | (ph << s);
+                    if (++s == S) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (!waited) flush();
+            if (!ok && leader) {
+                for (int i = 0; i < S; i++)
+                    if (issued >> i & 1u) {
+                        const uint32_t addr = smem_u32(&full_bar[i]);
+                        const uint64_t t0 = gtime_ns();
+                        while (!mbar_try(addr, (last_ph >> i) & 1u) && gtime_ns() - t0 < kTcuWaitCycles) {
+                        }
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (even CTA) ----------------
+            int s = 0, it = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int tile = cid; tile < total && ok; tile += ncl, it++) {
+                const int acc = it & 1;
+                const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+                if (!mbar_wait(&tempty_bar[acc], aph ^ 1u, abort_flag, a.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * kPairBN);
+                for (int kb = 0; kb < nkb; kb++) {
+                    if (!mbar_wait(&full_bar[s], ph, abort_flag, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
+                    const uint64_t bd = sw128_desc(smem_u32(sB + s * B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        tc_mma_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    tc_commit_pair(&empty_bar[s]);
+                    if (++s == S) { s = 0; ph ^= 1u; }
+                }
+                if (ok) tc_commit_pair(&tfull_bar[acc]);
+            }
+            tc_commit_pair(&done_bar);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+        griddep_wait();
+        const uint32_t tempty0 = cluster_map(smem_u32(&tempty_bar[0]), 0);
+        const int q = warp & 3;
+        int it = 0;
+        for (int tile = cid; tile < total; tile += ncl, it++) {
+            TileCoord c = pair_tile_coord(tile, nf, nt);
+            c.f0 += (int)rank * kBM;  // this CTA's 128 features
+            const int acc = it & 1;
+            const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+            if (!mbar_wait(&tfull_bar[acc], aph, abort_flag, a.err)) break;
+            tc_fence_after();
+            const int f = c.f0 + q * 32 + lane;
+            const int tbase = c.t0 * kPairBN;
+            const int ncols = min(kPairBN, a.T - tbase);
+            for (int cc = 0; cc < ncols; cc += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kPairBN + cc), r);
+                const int nj = min(32, ncols - cc);
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                tc_emit<EPI>(a, v, c, f, q, lane, tbase + cc, nj, 0, sStage);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * (uint32_t)acc);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1 && lane == 0) {
+        // every MMA of the pair has completed (they read both CTAs' shared memory and write both TMEMs)
+        const uint32_t addr = smem_u32(&done_bar);
+        const uint64_t t0 = gtime_ns();
+        while (!mbar_try(addr, 0) && gtime_ns() - t0 < kTcuWaitCycles) {
+        }
+    }
+    __syncthreads();
+    cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 // bf16 (rows, cols) row-major, box of box_rows x 64 columns, 128-byte swizzle, zero fill
@@ -344,6 +552,27 @@ cudaError_t launch_bn(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs
     const int total = nf * nt * a.ksplit;
     const int grid = total < num_sms ? total : num_sms;
     return launch_pdl(kfn, dim3(grid), dim3(kTcThreads), tc_smem_bytes(BN), st, mw, mx, a);
+}
+
+template <int EPI>
+cudaError_t launch_pair(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a, int num_sms, cudaStream_t st) {
+    const int total = ((a.M + kPairBM - 1) / kPairBM) * ((a.T + kPairBN - 1) / kPairBN);
+    const int ncl = total < num_sms / 2 ? total : num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * ncl);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = pair_smem(EPI);
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, qw_tc_gemm_pair_kernel<EPI>, mw, mx, a);
 }
 
 template <int EPI>
@@ -400,7 +629,9 @@ static cudaError_t prepare_epi() {
         cudaError_t e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes(bns[i]));
         if (e != cudaSuccess) return e;
     }
-    return cudaSuccess;
+    if (EPI == TC_ARGMAX) return cudaSuccess;
+    return cudaFuncSetAttribute((const void *)qw_tc_gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                pair_smem(EPI));
 }
 
 cudaError_t tc_prepare() {
@@ -409,6 +640,15 @@ cudaError_t tc_prepare() {
     if (e == cudaSuccess) e = prepare_epi<TC_SWIGLU>();
     if (e == cudaSuccess) e = prepare_epi<TC_ARGMAX>();
     return e;
+}
+
+// QW_TC_PAIR=0 keeps prefill shapes on the one-CTA kernel (A/B measurements)
+bool tc_pair_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("QW_TC_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 int tc_pick_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
@@ -441,6 +681,19 @@ cudaError_t tc_gemm_launch(const void *W, const void *X, const TcArgs &a, int ep
     if (epi == TC_RESID && a.ksplit > 1 && a.out != (const void *)a.resid) return cudaErrorInvalidValue;
     if (bn == 0) bn = tc_pick_bn(a.T);
     CUtensorMap mw, mx;
+    if (bn == 256 && a.ksplit == 1 && epi != TC_ARGMAX && tc_pair_enabled() &&
+        ((a.M + kPairBM - 1) / kPairBM) * ((a.T + kPairBN - 1) / kPairBN) >= num_sms / 2) {
+        // prefill shapes: the CTA-pair kernel (each CTA maps 128-row boxes of W and of X)
+        cudaError_t e = make_map(&mw, W, a.M, a.K, kBM);
+        if (e == cudaSuccess) e = make_map(&mx, X, a.T, a.K, kPairHalfN);
+        if (e != cudaSuccess) return e;
+        switch (epi) {
+            case TC_STORE: return launch_pair<TC_STORE>(mw, mx, a, num_sms, st);
+            case TC_RESID: return launch_pair<TC_RESID>(mw, mx, a, num_sms, st);
+            case TC_SWIGLU: return launch_pair<TC_SWIGLU>(mw, mx, a, num_sms, st);
+        }
+        return cudaErrorInvalidValue;
+    }
     cudaError_t e = make_map(&mw, W, a.M, a.K, kBM);
     if (e != cudaSuccess) return e;
     e = make_map(&mx, X, a.T, a.K, bn);

@@ -64,3 +64,43 @@ def test_linear_rejects_bad_shapes():
     with pytest.raises(native.QwenError) as e:
         native.op_linear(16, 64, 12, 16, 4, native.LINEAR_STORE, 0, 0, 16)
     assert e.value.status == 2
+
+
+# prefill shapes (>= 74 tiles of 256 x 256): the CTA-pair (cta_group::2) kernel, with a ragged token edge, k not a
+# multiple of 64 and feature counts whose last 256-row tile is partly or (for the odd CTA) wholly past the end
+@pytest.mark.parametrize("n_out,k,t", [(6144, 4096, 4096), (4000, 520, 2500), (4224, 200, 4700)])
+def test_linear_pair_store_matches_torch(n_out, k, t):
+    import torch
+    W, X = operands(n_out, k, t, seed=3)
+    bias = torch.randn(n_out, device="cuda")
+    out = torch.full((t, n_out), float("nan"), device="cuda")
+    native.op_linear(W.data_ptr(), n_out, k, X.data_ptr(), t, native.LINEAR_STORE, bias.data_ptr(), 0,
+                     out.data_ptr())
+    torch.cuda.synchronize()
+    want = X.float() @ W.float().t() + bias
+    assert rel(out, want) < 1e-4
+
+
+def test_linear_pair_resid_in_place():
+    import torch
+    n_out, k, t = 4096, 1024, 4700
+    W, X = operands(n_out, k, t, seed=4)
+    x = torch.randn(t, n_out, device="cuda")
+    want = x + X.float() @ W.float().t()
+    native.op_linear(W.data_ptr(), n_out, k, X.data_ptr(), t, native.LINEAR_RESID, 0, x.data_ptr(), x.data_ptr())
+    torch.cuda.synchronize()
+    assert rel(x, want) < 1e-5
+
+
+@pytest.mark.parametrize("n_out,t", [(8192, 2600), (4224, 4700)])
+def test_linear_pair_swiglu_interleaved(n_out, t):
+    import torch
+    k = 512
+    W, X = operands(n_out, k, t, seed=5)
+    out = torch.zeros(t, n_out // 2, dtype=torch.bfloat16, device="cuda")
+    native.op_linear(W.data_ptr(), n_out, k, X.data_ptr(), t, native.LINEAR_SWIGLU, 0, 0, out.data_ptr())
+    torch.cuda.synchronize()
+    y = (X.float() @ W.float().t()).view(t, n_out // 32, 2, 16)
+    gate, up = y[:, :, 0, :].reshape(t, -1), y[:, :, 1, :].reshape(t, -1)
+    want = up * torch.nn.functional.silu(gate)
+    assert rel(out.float(), want) < 1e-2
