@@ -71,6 +71,13 @@ struct QkvPostArgs {
     int H, Hkv, d;
     __nv_bfloat16 *q_out;  // (rows, ld_q) bf16 rotated queries
     int ld_q;
+    // optional (vector mode, tp > 1, rows <= SM count): the sums of squares exchanged over NVLink inside the
+    // kernel instead of qk_ss: flag-in-data words in every rank's inbox [rows][tp][2] at word offset xoff
+    unsigned long long *const *xpeers;
+    long long xoff;
+    int tp, rank;
+    unsigned *gen, *done;  // generation / CTA arrivals shared with the all-reduce kernels (qw_allreduce.cu)
+    int *err;
 };
 
 struct FlashArgs {

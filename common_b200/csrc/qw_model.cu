@@ -104,6 +104,8 @@ struct qw_model {
     unsigned long long **d_ar = nullptr;    // device array of all ranks' all-reduce inboxes
     unsigned *ar_ctr = nullptr;             // generation | CTA arrivals of the all-reduce kernel
     long long ar_cap = 0;                   // elements one all-reduce may carry
+    long long ar_xoff = 0;                  // word offset of the QK-norm sums inbox ([max_batch][tp][2]) in ar_buf
+    bool ar_fuse = true;                    // batched decode: all-reduce + rmsnorm and the QK sums in one kernel each
     unsigned *d_persist = nullptr;          // barrier generation + release word, persistent
     // sampling (qw_set_sampling): temperature <= 0 keeps greedy decoding
     double samp_temperature = 0.0, samp_top_p = 1.0;
@@ -552,22 +554,39 @@ qw_status tc_gemm(qw_model *m, int kind, const void *W, const void *X, int M, in
 // (flash attention); otherwise T single-token sequences (paged decode attention).  Leaves the
 // residual stream in m->xa and, under tensor parallelism, the last all-reduced partial in *pending.
 qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, const int *row_slot, const int *row_pos,
-                    bool prefill, int nseq, int p0, int L, const int *seq_slots, const float **pending_out) {
+                    bool prefill, int nseq, int p0, int L, const int *seq_slots, const float **pending_out,
+                    bool *final_normed = nullptr) {
     const qw_config &c = m->c;
     PrefillBuffers &pf = m->pf;
     const int D = m->D, d = c.head_dim;
     const bool tpm = m->tp > 1;
+    // tensor-parallel decode: each all-reduce fused with the residual update and the next rmsnorm (qw_ar_norm_kernel),
+    // the QK-norm sums exchanged inside qkv_post; the last layer's down all-reduce applies the final norm
+    const bool fuse = tpm && !prefill && m->ar_fuse && m->ar_buf && (long long)T * D <= m->ar_cap &&
+                      T <= m->num_sms && m->tp <= 8 && D % (4 * m->tp) == 0;
+    if (final_normed) *final_normed = fuse;
+    auto ar_norm = [&](float *part, const float *w) -> qw_status {
+        ArNormArgs an{};
+        an.part = part; an.ld_part = D; an.zero_part = part == m->part_split;
+        an.x = m->xa; an.w = w; an.eps = (float)c.eps; an.out = pf.act; an.ld_out = D; an.D = D; an.rows = T;
+        an.tp = m->tp; an.rank = m->rank; an.peers = m->d_ar; an.gen = m->ar_ctr; an.done = m->ar_ctr + 1;
+        an.err = pf.d_err;
+        LK(ar_norm_launch(an, m->num_sms, m->st));
+        return QW_OK;
+    };
     float *x = m->xa;
     const float *pending = nullptr;
     if (x_in) CK(cudaMemcpyAsync(x, x_in, sizeof(float) * (size_t)T * D, cudaMemcpyDeviceToDevice, m->st));
     for (int l = 0; l < c.layers; l++) {
         Layer &Ly = m->L[l];
-        // ---- residual update + rmsnorm -> bf16 rows ----
+        // ---- residual update + rmsnorm -> bf16 rows (fused: done by the previous layer's last all-reduce) ----
         NormRowsArgs na{};
-        na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
-        if (l == 0 && !x_in) { na.embed = (const __nv_bfloat16 *)m->embed; na.tokens = tokens; }
-        na.w = Ly.rms_att; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
-        LK(norm_rows_launch(na, T, m->st));
+        if (!fuse || l == 0) {
+            na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
+            if (l == 0 && !x_in) { na.embed = (const __nv_bfloat16 *)m->embed; na.tokens = tokens; }
+            na.w = Ly.rms_att; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
+            LK(norm_rows_launch(na, T, m->st));
+        }
         pending = nullptr;
         // ---- fused QKV projection ----
         // split K (skinny decode shapes): atomics into qkv_split, which qkv_post zeroes again after reading it
@@ -576,7 +595,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         TRY(tc_gemm(m, QW_KERNEL_QKV, Ly.w_qkv, pf.act, m->QKVl, T, D, TC_STORE, qkv, m->QKVl, nullptr, Ly.b_qkv,
                     qkv_sp));
         const float *qk_ss = nullptr;
-        if (tpm && c.qk_norm == QW_QKNORM_VECTOR) {
+        if (tpm && c.qk_norm == QW_QKNORM_VECTOR && !fuse) {
             LK(qk_sumsq_launch(qkv, m->QKVl, m->Ql, m->KVl, T, pf.row_ss, m->st));
             TRY(allreduce(m, pf.row_ss, (size_t)T * 2));
             qk_ss = pf.row_ss;
@@ -590,6 +609,10 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             qa.slots = row_slot; qa.positions = row_pos; qa.page_table = m->d_page_table; qa.max_pages = m->max_pages;
             qa.page_size = m->page_size; qa.log2_page = m->log2_page; qa.kcache = kc; qa.vcache = vc;
             qa.H = m->Hl; qa.Hkv = m->Hkvl; qa.d = d; qa.q_out = pf.q; qa.ld_q = m->Ql;
+            if (fuse && c.qk_norm == QW_QKNORM_VECTOR) {
+                qa.xpeers = m->d_ar; qa.xoff = m->ar_xoff; qa.tp = m->tp; qa.rank = m->rank;
+                qa.gen = m->ar_ctr; qa.done = m->ar_ctr + 1; qa.err = pf.d_err;
+            }
             LK(qkv_post_launch(qa, T, m->bf16kv, m->st));
         }
         if (prefill) {
@@ -617,16 +640,22 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             const bool sp = !prefill && T <= m->B;
             float *pb = sp ? m->part_split : m->part;
             TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, pb, D, nullptr, nullptr, sp));
-            TRY(allreduce(m, pb, (size_t)T * D));
-            pending = pb;
+            if (fuse) {
+                TRY(ar_norm(pb, Ly.rms_ffn));
+            } else {
+                TRY(allreduce(m, pb, (size_t)T * D));
+                pending = pb;
+            }
         } else {
             TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_RESID, x, D, x, nullptr, true));
         }
         // ---- residual update + rmsnorm ----
-        na = NormRowsArgs{};
-        na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
-        na.w = Ly.rms_ffn; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
-        LK(norm_rows_launch(na, T, m->st));
+        if (!fuse) {
+            na = NormRowsArgs{};
+            na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
+            na.w = Ly.rms_ffn; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
+            LK(norm_rows_launch(na, T, m->st));
+        }
         pending = nullptr;
         // ---- gate/up + SwiGLU, down (+ residual) ----
         if (!prefill && T <= m->B && m->gu_split && tc_pick_ksplit(2 * m->Fl, T, D, tc_pick_bn(T), m->num_sms) > 1) {
@@ -644,8 +673,12 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             const bool sp = !prefill && T <= m->B;
             float *pb = sp ? m->part_split : m->part;
             TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, pb, D, nullptr, nullptr, sp));
-            TRY(allreduce(m, pb, (size_t)T * D));
-            pending = pb;
+            if (fuse) {
+                TRY(ar_norm(pb, l + 1 < c.layers ? m->L[l + 1].rms_att : m->norm_final));
+            } else {
+                TRY(allreduce(m, pb, (size_t)T * D));
+                pending = pb;
+            }
         } else {
             TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_RESID, x, D, x, nullptr, true));
         }
@@ -658,12 +691,15 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
 qw_status tc_decode(qw_model *m, int *tokens, const float *x_in, const int *slots, int *positions, int B,
                     float *logits_out_dev, int *argmax_dev, int advance, int *hist, int hist_ld) {
     const float *pending = nullptr;
-    TRY(tc_layers(m, B, tokens, x_in, slots, positions, false, 0, 0, 1, nullptr, &pending));
+    bool normed = false;
+    TRY(tc_layers(m, B, tokens, x_in, slots, positions, false, 0, 0, 1, nullptr, &pending, &normed));
     const bool tpm = m->tp > 1;
-    NormRowsArgs na{};
-    na.x = m->xa; na.ld_x = m->D; na.part = const_cast<float *>(pending); na.ld_part = m->D; na.zero_part = pending == m->part_split;
-    na.w = m->norm_final; na.eps = (float)m->c.eps; na.out = m->pf.act; na.ld_out = m->D; na.K = m->D;
-    LK(norm_rows_launch(na, B, m->st));
+    if (!normed) {
+        NormRowsArgs na{};
+        na.x = m->xa; na.ld_x = m->D; na.part = const_cast<float *>(pending); na.ld_part = m->D; na.zero_part = pending == m->part_split;
+        na.w = m->norm_final; na.eps = (float)m->c.eps; na.out = m->pf.act; na.ld_out = m->D; na.K = m->D;
+        LK(norm_rows_launch(na, B, m->st));
+    }
     // lm_head with the argmax candidates of every 32 vocabulary rows in its epilogue; logits only when asked for
     float *lg = logits_out_dev ? (tpm ? m->logits : logits_out_dev) : nullptr;
     const int ncand = (m->Vl + 127) / 128 * 4;
@@ -907,7 +943,10 @@ static qw_status setup_exchange(qw_model *m) {
 // Inboxes of the batched decode step's all-reduce (qw_allreduce.cu): up to max_batch x dim elements.
 static qw_status setup_allreduce(qw_model *m) {
     m->ar_cap = (long long)m->B * m->D;
-    const size_t words = (size_t)allreduce_ll_words(m->ar_cap, m->tp);
+    m->ar_xoff = (allreduce_ll_words(m->ar_cap, m->tp) + 1) & ~1ll;  // 16-byte aligned pairs of words
+    const size_t words = (size_t)m->ar_xoff + (size_t)2 * m->B * m->tp;
+    const char *fe = getenv("QW_AR_FUSE");
+    m->ar_fuse = !(fe && fe[0] == '0');
     qw_status s = open_peer_buffer(m, words * 8, (void **)&m->ar_buf, m->xch_peer, (void ***)&m->d_ar);
     if (s) return s;
     AL(m->ar_ctr, 2);

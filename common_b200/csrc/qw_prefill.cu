@@ -13,6 +13,7 @@
 //   rows_argmax   first index of the maximum of each logits row (AggregationFeatures.java:111-121).
 #include "qw_internal.cuh"
 #include "qw_kernels.h"
+#include "qw_ar.h"
 #include "qw_tc.h"
 #include "qw_tc_util.cuh"
 #include <float.h>
@@ -79,6 +80,7 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
 // qkv_post: one CTA per token row
 // ------------------------------------------------------------------------------------------
 constexpr int kPostThreads = 512;
+constexpr unsigned long long kXwWaitCycles = 4000ull * 1000ull * 1000ull;  // ~2 s at 2 GHz
 
 template <typename KT>
 __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a) {
@@ -90,6 +92,7 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
     const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int d = a.d, Ql = a.H * d, KVl = a.Hkv * d, W = Ql + 2 * KVl;
     const float *src = a.qkv + (size_t)r * a.ld_qkv;
+    unsigned xgen = 0;  // thread 0: generation of the sums exchange
     float sq = 0.f, sk = 0.f;
     for (int i = tid; i < W; i += kPostThreads) {
         float v = src[i];
@@ -112,6 +115,34 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
             float tq = 0.f, tk = 0.f;
             for (int w = 0; w < kPostThreads / 32; w++) { tq += red[0][w]; tk += red[1][w]; }
             if (a.qk_ss) { tq = a.qk_ss[2 * r]; tk = a.qk_ss[2 * r + 1]; }
+            if (a.xpeers) {
+                // every rank's two sums of this row, added in rank order (the same scale on every rank)
+                xgen = *reinterpret_cast<volatile unsigned *>(a.gen) + 1u;
+                for (int p = 0; p < a.tp; p++) {
+                    unsigned long long *dst = a.xpeers[p] + a.xoff + ((size_t)r * a.tp + a.rank) * 2;
+                    xw_store(dst, tq, xgen);
+                    xw_store(dst + 1, tk, xgen);
+                }
+                const unsigned long long *in = a.xpeers[a.rank] + a.xoff + (size_t)r * a.tp * 2;
+                float sq2 = 0.f, sk2 = 0.f;
+                bool ok = true;
+                unsigned long long w[8][2];  // every rank's pair loaded at once (tp <= 8), then settled in order
+#pragma unroll
+                for (int p = 0; p < 8; p++)
+                    if (p < a.tp) xw_load2(in + 2 * p, w[p][0], w[p][1]);
+#pragma unroll
+                for (int p = 0; p < 8; p++)
+                    if (p < a.tp && ok) {
+                        float vq = 0.f, vk = 0.f;
+                        ok = xw_settle(in + 2 * p, w[p][0], xgen, vq, kXwWaitCycles) &&
+                             xw_settle(in + 2 * p + 1, w[p][1], xgen, vk, kXwWaitCycles);
+                        sq2 += vq;
+                        sk2 += vk;
+                    }
+                if (!ok && a.err) atomicExch(a.err, 6);
+                tq = sq2;
+                tk = sk2;
+            }
             s_sc[0] = 1.0f / sqrtf(tq / (float)a.q_total + 1e-6f);
             s_sc[1] = 1.0f / sqrtf(tk / (float)a.kv_total + 1e-6f);
         }
@@ -154,6 +185,17 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
         const size_t off = (((size_t)page * a.Hkv + h) * a.page_size + (pos & (a.page_size - 1))) * d + j;
         Elt<KT>::store(kc + off, row[Ql + i]);
         Elt<KT>::store(vc + off, row[Ql + KVl + i]);
+    }
+    if (a.xpeers && a.qk_mode == 1) {
+        // the last CTA advances the exchange generation (every CTA has read it)
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            if (atomicAdd(a.done, 1u) == gridDim.x - 1) {
+                *a.done = 0u;
+                *a.gen = xgen;
+            }
+        }
     }
 }
 
