@@ -344,18 +344,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------------------------
 constexpr int kPairBM = 256, kPairBN = 256, kPairHalfN = 128;
 constexpr int kPairStageBytes = (kBM + kPairHalfN) * kBK * 2;
+constexpr int kPairGroupT = 8;  // token tiles per group of the tile order (their X tiles stay in L2)
 // seven stages (224 KB) where the epilogue stages nothing in shared memory, six beside SWIGLU's 4 KB rows
 __host__ __device__ constexpr int pair_stages(int epi) { return epi == TC_SWIGLU ? 6 : 7; }
 __host__ __device__ constexpr int pair_smem(int epi) {
     return pair_stages(epi) * kPairStageBytes + 1024 + (epi == TC_SWIGLU ? 4096 : 0);
 }
 
-__device__ __forceinline__ TileCoord pair_tile_coord(int tile, int nf, int nt) {
+__device__ __forceinline__ TileCoord pair_tile_coord(int tile, int nf, int nt, int gt) {
     TileCoord c;
-    const int per_group = nf * kGroupT;
+    const int per_group = nf * gt;
     const int g = tile / per_group, r = tile % per_group;
-    const int t_in = min(kGroupT, nt - g * kGroupT);
-    c.t0 = g * kGroupT + r % t_in;
+    const int t_in = min(gt, nt - g * gt);
+    c.t0 = g * gt + r % t_in;
     c.f0 = (r / t_in) * kPairBM;
     c.ks = 0;
     c.kb0 = 0;
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tma_load_2d_pair(sB + i * B_BYTES, &tmX, full0 + 8u * i, pend_kb[i] * kBK, pend_t[i]);
             };
             for (int tile = cid; tile < total && ok; tile += ncl) {
-                const TileCoord c = pair_tile_coord(tile, nf, nt);
+                const TileCoord c = pair_tile_coord(tile, nf, nt, a.group_t);
                 const int wrow = c.f0 + (int)rank * kBM, trow = c.t0 * kPairBN + (int)rank * kPairHalfN;
                 for (int kb = 0; kb < nkb; kb++) {
                     if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag, a.err)) { ok = false; break; }
@@ -496,7 +497,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int q = warp & 3;
         int it = 0;
         for (int tile = cid; tile < total; tile += ncl, it++) {
-            TileCoord c = pair_tile_coord(tile, nf, nt);
+            TileCoord c = pair_tile_coord(tile, nf, nt, a.group_t);
             c.f0 += (int)rank * kBM;  // this CTA's 128 features
             const int acc = it & 1;
             const uint32_t aph = (uint32_t)(it >> 1) & 1u;
@@ -555,7 +556,13 @@ cudaError_t launch_bn(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs
 }
 
 template <int EPI>
-cudaError_t launch_pair(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a, int num_sms, cudaStream_t st) {
+cudaError_t launch_pair(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &a_in, int num_sms, cudaStream_t st) {
+    TcArgs a = a_in;
+    static const int gt_env = [] {
+        const char *e = getenv("QW_TC_GROUP");
+        return e ? atoi(e) : 0;
+    }();
+    a.group_t = gt_env > 0 ? gt_env : kPairGroupT;
     const int total = ((a.M + kPairBM - 1) / kPairBM) * ((a.T + kPairBN - 1) / kPairBN);
     const int ncl = total < num_sms / 2 ? total : num_sms / 2;
     cudaLaunchConfig_t cfg = {};

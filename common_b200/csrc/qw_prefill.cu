@@ -24,7 +24,7 @@ namespace qw {
 // ------------------------------------------------------------------------------------------
 // norm_rows: one CTA per token row
 // ------------------------------------------------------------------------------------------
-constexpr int kNormThreads = 512;
+constexpr int kNormThreads = 256;  // 8 rows per SM in flight (16 KB of shared memory each)
 constexpr size_t kPrepSmem = 160 * 1024;  // dynamic shared memory the row kernels are opted in to
 
 __global__ void __launch_bounds__(kNormThreads) qw_norm_rows_kernel(NormRowsArgs a) {
@@ -79,9 +79,27 @@ cudaError_t norm_rows_launch(const NormRowsArgs &a, int rows, cudaStream_t st) {
 // ------------------------------------------------------------------------------------------
 // qkv_post: one CTA per token row
 // ------------------------------------------------------------------------------------------
-constexpr int kPostThreads = 512;
+constexpr int kPostThreads = 256;
 constexpr unsigned long long kXwWaitCycles = 4000ull * 1000ull * 1000ull;  // ~2 s at 2 GHz
 
+// 8 consecutive values to the cache type: one 16-byte store (bf16) or two (fp32)
+__device__ __forceinline__ void store8(__nv_bfloat16 *p, const float (&v)[8]) {
+    uint4 u;
+    u.x = (uint32_t)f2bf_bits(v[0]) | ((uint32_t)f2bf_bits(v[1]) << 16);
+    u.y = (uint32_t)f2bf_bits(v[2]) | ((uint32_t)f2bf_bits(v[3]) << 16);
+    u.z = (uint32_t)f2bf_bits(v[4]) | ((uint32_t)f2bf_bits(v[5]) << 16);
+    u.w = (uint32_t)f2bf_bits(v[6]) | ((uint32_t)f2bf_bits(v[7]) << 16);
+    *reinterpret_cast<uint4 *>(p) = u;
+}
+__device__ __forceinline__ void store8(float *p, const float (&v)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// One row: QK-norm (AttentionFeatures.java:840-845, 886-891 whole-vector; or per head), split-half RoPE
+// (RotationFeatures.java:189-208) of q and k, bf16 queries out, k and v into the paged cache.  The row is
+// loaded once (16-byte loads) into shared memory; then one pass in which a thread takes 8 columns of the first
+// half of a head together with the matching 8 of its second half (a RoPE pair), or 8 columns of v.
 template <typename KT>
 __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a) {
     griddep_launch_dependents();  // programmatic launch: the next kernel may start its prologue
@@ -89,16 +107,18 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
     extern __shared__ __align__(16) float row[];  // q (Ql) | k (KVl) | v (KVl)
     __shared__ float red[2][kPostThreads / 32];
     __shared__ float s_sc[2];
+    __shared__ float s_head[128];  // per-head scales (qk_mode 2)
     const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int d = a.d, Ql = a.H * d, KVl = a.Hkv * d, W = Ql + 2 * KVl;
     const float *src = a.qkv + (size_t)r * a.ld_qkv;
     unsigned xgen = 0;  // thread 0: generation of the sums exchange
     float sq = 0.f, sk = 0.f;
-    for (int i = tid; i < W; i += kPostThreads) {
-        float v = src[i];
-        row[i] = v;
-        if (i < Ql) sq += v * v;
-        else if (i < Ql + KVl) sk += v * v;
+    for (int i = tid * 4; i < W; i += kPostThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(src + i);
+        *reinterpret_cast<float4 *>(row + i) = v;
+        const float s2 = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        if (i < Ql) sq += s2;
+        else if (i < Ql + KVl) sk += s2;
     }
     if (a.zero_qkv) {
         // zeroed again for the next split-K accumulation into this buffer (after all loads of the row)
@@ -146,45 +166,80 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
             s_sc[0] = 1.0f / sqrtf(tq / (float)a.q_total + 1e-6f);
             s_sc[1] = 1.0f / sqrtf(tk / (float)a.kv_total + 1e-6f);
         }
-        __syncthreads();
-        const float scq = s_sc[0], sck = s_sc[1];
-        for (int i = tid; i < Ql + KVl; i += kPostThreads)
-            row[i] = i < Ql ? a.qn[i] * row[i] * scq : a.kn[i - Ql] * row[i] * sck;
     } else if (a.qk_mode == 2) {
         __syncthreads();
         for (int hh = warp; hh < a.H + a.Hkv; hh += kPostThreads / 32) {
-            float *v = row + (size_t)hh * d;
-            const float *w = hh < a.H ? a.qn + (size_t)hh * d : a.kn + (size_t)(hh - a.H) * d;
-            float s = 0.f;
-            for (int i = lane; i < d; i += 32) s += v[i] * v[i];
-            s = warp_sum(s);
-            const float sc = 1.0f / sqrtf(s / (float)d + 1e-6f);
-            for (int i = lane; i < d; i += 32) v[i] = w[i] * v[i] * sc;
+            const float *v = row + (size_t)hh * d;
+            float s2 = 0.f;
+            for (int i = lane; i < d; i += 32) s2 += v[i] * v[i];
+            s2 = warp_sum(s2);
+            if (lane == 0) s_head[hh] = 1.0f / sqrtf(s2 / (float)d + 1e-6f);
         }
     }
     __syncthreads();
     const int pos = a.positions[r];
-    const int half = d / 2;
+    const int half = d / 2, hc = half / 8;  // 8-column pieces per half head
     const float2 *fr = a.freq + (size_t)pos * half;
-    for (int i = tid; i < (a.H + a.Hkv) * half; i += kPostThreads) {
-        const int hh = i / half, f = i % half;
-        float *v = row + (size_t)hh * d;
-        const float2 cs = fr[f];
-        const float x1 = v[f], x2 = v[f + half];
-        v[f] = x1 * cs.x - x2 * cs.y;
-        v[f + half] = x2 * cs.x + x1 * cs.y;
-    }
-    __syncthreads();
-    for (int i = tid; i < Ql; i += kPostThreads) a.q_out[(size_t)r * a.ld_q + i] = __float2bfloat16_rn(row[i]);
     const int slot = a.slots[r];
     const int page = a.page_table[(size_t)slot * a.max_pages + (pos >> a.log2_page)];
+    const size_t cache_row = ((size_t)page * a.Hkv * a.page_size + (pos & (a.page_size - 1))) * d;
     KT *kc = reinterpret_cast<KT *>(a.kcache);
     KT *vc = reinterpret_cast<KT *>(a.vcache);
-    for (int i = tid; i < KVl; i += kPostThreads) {
-        const int h = i / d, j = i % d;
-        const size_t off = (((size_t)page * a.Hkv + h) * a.page_size + (pos & (a.page_size - 1))) * d + j;
-        Elt<KT>::store(kc + off, row[Ql + i]);
-        Elt<KT>::store(vc + off, row[Ql + KVl + i]);
+    const int nrope = (a.H + a.Hkv) * hc, nv = KVl / 8;
+    for (int it = tid; it < nrope + nv; it += kPostThreads) {
+        if (it < nrope) {
+            const int hh = it / hc, f0 = (it % hc) * 8;
+            const bool isq = hh < a.H;
+            const float *v = row + (size_t)hh * d;
+            float x1[8], x2[8];
+#pragma unroll
+            for (int e = 0; e < 8; e += 4) {
+                const float4 u1 = *reinterpret_cast<const float4 *>(v + f0 + e);
+                const float4 u2 = *reinterpret_cast<const float4 *>(v + f0 + half + e);
+                x1[e] = u1.x; x1[e + 1] = u1.y; x1[e + 2] = u1.z; x1[e + 3] = u1.w;
+                x2[e] = u2.x; x2[e + 1] = u2.y; x2[e + 2] = u2.z; x2[e + 3] = u2.w;
+            }
+            if (a.qk_mode == 1) {
+                const float sc = isq ? s_sc[0] : s_sc[1];
+                const float *w = isq ? a.qn + (size_t)hh * d : a.kn + (size_t)(hh - a.H) * d;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    x1[e] = w[f0 + e] * x1[e] * sc;
+                    x2[e] = w[f0 + half + e] * x2[e] * sc;
+                }
+            } else if (a.qk_mode == 2) {
+                const float sc = s_head[hh];
+                const float *w = isq ? a.qn + (size_t)hh * d : a.kn + (size_t)(hh - a.H) * d;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    x1[e] = w[f0 + e] * x1[e] * sc;
+                    x2[e] = w[f0 + half + e] * x2[e] * sc;
+                }
+            }
+            float y1[8], y2[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float2 cs = fr[f0 + e];
+                y1[e] = x1[e] * cs.x - x2[e] * cs.y;
+                y2[e] = x2[e] * cs.x + x1[e] * cs.y;
+            }
+            if (isq) {
+                __nv_bfloat16 *q = a.q_out + (size_t)r * a.ld_q + (size_t)hh * d;
+                store8(q + f0, y1);
+                store8(q + f0 + half, y2);
+            } else {
+                KT *k = kc + cache_row + (size_t)(hh - a.H) * a.page_size * d;
+                store8(k + f0, y1);
+                store8(k + f0 + half, y2);
+            }
+        } else {
+            const int c = (it - nrope) * 8, h = c / d, j = c % d;
+            const float *v = row + Ql + KVl + c;
+            float x[8];
+            const float4 u1 = *reinterpret_cast<const float4 *>(v), u2 = *reinterpret_cast<const float4 *>(v + 4);
+            x[0] = u1.x; x[1] = u1.y; x[2] = u1.z; x[3] = u1.w; x[4] = u2.x; x[5] = u2.y; x[6] = u2.z; x[7] = u2.w;
+            store8(vc + cache_row + (size_t)h * a.page_size * d + j, x);
+        }
     }
     if (a.xpeers && a.qk_mode == 1) {
         // the last CTA advances the exchange generation (every CTA has read it)
@@ -201,6 +256,7 @@ __global__ void __launch_bounds__(kPostThreads) qw_qkv_post_kernel(QkvPostArgs a
 
 cudaError_t qkv_post_launch(const QkvPostArgs &a, int rows, bool kv_bf16, cudaStream_t st) {
     size_t smem = sizeof(float) * (size_t)(a.H + 2 * a.Hkv) * a.d;
+    if (a.d % 16 || a.H + a.Hkv > 128 || a.ld_qkv % 4 || a.ld_q % 8) return cudaErrorInvalidValue;
     auto k16 = qw_qkv_post_kernel<__nv_bfloat16>;
     auto k32 = qw_qkv_post_kernel<float>;
     if (smem > kPrepSmem) return cudaErrorInvalidValue;

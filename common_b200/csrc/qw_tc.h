@@ -37,6 +37,7 @@ struct TcArgs {
     float *cand_val;    // ARGMAX: (T, ncand) per-group maxima and their feature indices
     int *cand_idx;
     int ncand;
+    int group_t;        // CTA-pair kernel: token tiles per group of its tile order (set by the launcher)
 };
 
 // Build the TMA descriptors and launch.  bn = 0 picks the token tile from T.
