@@ -590,7 +590,8 @@ def run_case(args):
     """Small fixed workloads for profiler captures (a few GB on the device, few launches):
       step-small  the 8B geometry cut to --layers layers, 4 batch-1 decode steps (the persistent step kernel)
       gemm        one qw_op_linear GEMM (--gemm M K T EPI) timed with CUDA events
-      attn-b64    the 8B geometry cut to 2 layers, 64 sequences prefilled to 2048 tokens, 3 batch-64 decode steps
+      attn-b64    the 8B geometry cut to 2 layers, --decode-batch (64) sequences prefilled to 2048 tokens, 3 batched
+                  decode steps
       prefill-small  the 8B geometry cut to 2 layers, two prefills of 8 x 4096 tokens
     """
     import numpy as np
@@ -637,7 +638,7 @@ def run_case(args):
         print(json.dumps({"case": args.case, "ok": True}))
         return 0
     layers = args.layers if args.case == "step-small" else 2
-    B, L = (1, 1024) if args.case == "step-small" else (64, 2048)
+    B, L = (1, 1024) if args.case == "step-small" else (args.decode_batch, 2048)
     cfg = native.make_config(g["dim"], g["hidden_dim"], layers, g["heads"], g["kv_heads"], g["head_dim"], g["vocab"],
                              L + 16, False, native.QKNORM_VECTOR, False, native.DTYPE_BF16, native.DTYPE_BF16, B,
                              16384 if B > 1 else 0)

@@ -363,13 +363,25 @@ int choose_nsplit(qw_model *m, int B) {
 int choose_flash_split(qw_model *m, int B) {
     const int per = B * m->Hkvl;
     const int resident = 2 * m->num_sms;
-    const int hi = std::max(1, std::min((m->c.seq_len + 63) / 64, m->maxsplit));
+    const int ntiles = (m->c.seq_len + 63) / 64;  // 64-key tiles at the longest context
+    const int hi = std::max(1, std::min(ntiles, m->maxsplit));
+    // QW_FLASH_FIXED overrides the fixed cost (a negative value restores the older waves / splits model)
+    static const double fixed = [] {
+        const char *e = getenv("QW_FLASH_FIXED");
+        return e ? atof(e) : 4.0;
+    }();
     int best_ns = 1;
     double best = 1e30;
     for (int ns = 1; ns <= hi; ns++) {
         const double waves = (double)(((long long)per * ns + resident - 1) / resident);
-        const double cost = waves / ns + 0.005 * ns;
-        if (cost < best) { best = cost; best_ns = ns; }
+        double cost;
+        if (fixed >= 0) {
+            // waves x (tiles per CTA + a CTA's fixed cost in tiles: set-up, first-load latency, split merge)
+            cost = waves * ((ntiles + ns - 1) / ns + fixed);
+        } else {
+            cost = waves / ns + 0.005 * ns;
+        }
+        if (cost < best - 1e-9) { best = cost; best_ns = ns; }
     }
     return best_ns;
 }
