@@ -106,6 +106,7 @@ struct qw_model {
     long long ar_cap = 0;                   // elements one all-reduce may carry
     long long ar_xoff = 0;                  // word offset of the QK-norm sums inbox ([max_batch][tp][2]) in ar_buf
     bool ar_fuse = true;                    // batched decode: all-reduce + rmsnorm and the QK sums in one kernel each
+    bool prefill_sp = true;                 // tensor-parallel prefill: reduce-scatter / row-block norm / all-gather
     unsigned *d_persist = nullptr;          // barrier generation + release word, persistent
     // sampling (qw_set_sampling): temperature <= 0 keeps greedy decoding
     double samp_temperature = 0.0, samp_top_p = 1.0;
@@ -567,7 +568,7 @@ qw_status tc_gemm(qw_model *m, int kind, const void *W, const void *X, int M, in
 // residual stream in m->xa and, under tensor parallelism, the last all-reduced partial in *pending.
 qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, const int *row_slot, const int *row_pos,
                     bool prefill, int nseq, int p0, int L, const int *seq_slots, const float **pending_out,
-                    bool *final_normed = nullptr) {
+                    bool *final_normed = nullptr, bool *seq_par = nullptr) {
     const qw_config &c = m->c;
     PrefillBuffers &pf = m->pf;
     const int D = m->D, d = c.head_dim;
@@ -577,6 +578,27 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
     const bool fuse = tpm && !prefill && m->ar_fuse && m->ar_buf && (long long)T * D <= m->ar_cap &&
                       T <= m->num_sms && m->tp <= 8 && D % (4 * m->tp) == 0;
     if (final_normed) *final_normed = fuse;
+    // tensor-parallel prefill, sequence-parallel between the projections: the O / down partials are reduce-scattered
+    // (each rank gets its block of T / tp rows summed), the residual update and rmsnorm run on that block only, and
+    // the normalised bf16 rows are all-gathered as the next projection's operand: 3/4 of an fp32 all-reduce's bytes
+    // and 1/tp of the row work.  The residual stream is then current only in this rank's row block.
+    const bool sp = tpm && prefill && m->prefill_sp && T % m->tp == 0;
+    if (seq_par) *seq_par = sp;
+    const int Tl = sp ? T / m->tp : T, rb = sp ? m->rank * Tl : 0;  // this rank's row block
+    auto sp_norm = [&](const float *part, const float *w, const int *tok) -> qw_status {
+        NormRowsArgs nb{};
+        nb.x = m->xa + (size_t)rb * D; nb.ld_x = D; nb.part = const_cast<float *>(part); nb.ld_part = D;
+        if (tok) { nb.embed = (const __nv_bfloat16 *)m->embed; nb.tokens = tok + rb; }
+        nb.w = w; nb.eps = (float)c.eps; nb.out = pf.act + (size_t)rb * D; nb.ld_out = D; nb.K = D;
+        LK(norm_rows_launch(nb, Tl, m->st));
+        NK(ncclAllGather(pf.act + (size_t)rb * D, pf.act, (size_t)Tl * D, ncclBfloat16, m->comm, m->st));
+        return QW_OK;
+    };
+    auto sp_reduce = [&](float *part) -> qw_status {
+        NK(ncclReduceScatter(part, part + (size_t)rb * D, (size_t)Tl * D, ncclFloat, ncclSum, m->comm, m->st));
+        return QW_OK;
+    };
+    const float *sp_pending = nullptr;  // this rank's block of the last reduce-scattered partial
     auto ar_norm = [&](float *part, const float *w) -> qw_status {
         ArNormArgs an{};
         an.part = part; an.ld_part = D; an.zero_part = part == m->part_split;
@@ -593,7 +615,10 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         Layer &Ly = m->L[l];
         // ---- residual update + rmsnorm -> bf16 rows (fused: done by the previous layer's last all-reduce) ----
         NormRowsArgs na{};
-        if (!fuse || l == 0) {
+        if (sp) {
+            TRY(sp_norm(sp_pending, Ly.rms_att, l == 0 ? tokens : nullptr));
+            sp_pending = nullptr;
+        } else if (!fuse || l == 0) {
             na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
             if (l == 0 && !x_in) { na.embed = (const __nv_bfloat16 *)m->embed; na.tokens = tokens; }
             na.w = Ly.rms_att; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
@@ -649,11 +674,14 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         // ---- O projection (+ residual) ----
         if (tpm) {
             // decode: split K with atomics into part_split, which the next rmsnorm zeroes again after reading it
-            const bool sp = !prefill && T <= m->B;
-            float *pb = sp ? m->part_split : m->part;
-            TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, pb, D, nullptr, nullptr, sp));
+            const bool ksp = !prefill && T <= m->B;
+            float *pb = ksp ? m->part_split : m->part;
+            TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_STORE, pb, D, nullptr, nullptr, ksp));
             if (fuse) {
                 TRY(ar_norm(pb, Ly.rms_ffn));
+            } else if (sp) {
+                TRY(sp_reduce(pb));
+                TRY(sp_norm(pb + (size_t)rb * D, Ly.rms_ffn, nullptr));
             } else {
                 TRY(allreduce(m, pb, (size_t)T * D));
                 pending = pb;
@@ -662,7 +690,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             TRY(tc_gemm(m, QW_KERNEL_O, Ly.w_o, pf.act, D, T, m->Ql, TC_RESID, x, D, x, nullptr, true));
         }
         // ---- residual update + rmsnorm ----
-        if (!fuse) {
+        if (!fuse && !sp) {
             na = NormRowsArgs{};
             na.x = x; na.ld_x = D; na.part = const_cast<float *>(pending); na.ld_part = D; na.zero_part = pending == m->part_split;
             na.w = Ly.rms_ffn; na.eps = (float)c.eps; na.out = pf.act; na.ld_out = D; na.K = D;
@@ -682,11 +710,14 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
         }
         if (tpm) {
             // decode: split K with atomics into part_split, which the next rmsnorm zeroes again after reading it
-            const bool sp = !prefill && T <= m->B;
-            float *pb = sp ? m->part_split : m->part;
-            TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, pb, D, nullptr, nullptr, sp));
+            const bool ksp = !prefill && T <= m->B;
+            float *pb = ksp ? m->part_split : m->part;
+            TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_STORE, pb, D, nullptr, nullptr, ksp));
             if (fuse) {
                 TRY(ar_norm(pb, l + 1 < c.layers ? m->L[l + 1].rms_att : m->norm_final));
+            } else if (sp) {
+                TRY(sp_reduce(pb));
+                sp_pending = pb + (size_t)rb * D;
             } else {
                 TRY(allreduce(m, pb, (size_t)T * D));
                 pending = pb;
@@ -695,7 +726,7 @@ qw_status tc_layers(qw_model *m, int T, const int *tokens, const float *x_in, co
             TRY(tc_gemm(m, QW_KERNEL_DOWN, Ly.w_down, pf.h, D, T, m->Fl, TC_RESID, x, D, x, nullptr, true));
         }
     }
-    *pending_out = pending;
+    *pending_out = sp ? sp_pending : pending;
     return QW_OK;
 }
 
@@ -827,6 +858,7 @@ qw_status tc_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, i
     const int Tmax = m->T;
     int *pin = pf.h_pin;
     const float *pending = nullptr;
+    bool seq_par = false;
     int L = 0;
     m->launches = 0;
     for (int p0 = 0; p0 < seq_len; p0 += Lc) {
@@ -843,16 +875,35 @@ qw_status tc_prefill(qw_model *m, const int32_t *tokens, const int32_t *slots, i
             }
         }
         CK(cudaMemcpyAsync(pf.row_slot, pin, sizeof(int) * (size_t)(3 * Tmax + batch), cudaMemcpyHostToDevice, m->st));
-        TRY(tc_layers(m, T, pf.row_tok, nullptr, pf.row_slot, pf.row_pos, true, batch, p0, L, pf.seq_slots, &pending));
+        TRY(tc_layers(m, T, pf.row_tok, nullptr, pf.row_slot, pf.row_pos, true, batch, p0, L, pf.seq_slots, &pending,
+                      nullptr, &seq_par));
     }
     // last position of every sequence: row b*L + L-1 of the final chunk
     float *dlog = nullptr;
     if (logits_out) dlog = m->logits_all ? m->logits_all + (size_t)m->tp * m->B * m->Vl : m->logits;
-    const size_t ld = (size_t)L * m->D;
+    const float *xl = m->xa, *pl = pending;
+    size_t ld = (size_t)L * m->D;
+    if (seq_par) {
+        // the residual rows are current only in their owner's row block: each owner puts x + its partial of those
+        // rows into a (batch, D) buffer, zeros elsewhere, and a sum over the ranks gives every rank all of them
+        const int T = batch * L, Tl = T / m->tp, rb = m->rank * Tl;
+        float *rows = pf.x_host_stage;
+        LK(zero_launch(rows, (size_t)batch * m->D, m->st));
+        for (int b = 0; b < batch; b++) {
+            const int r = b * L + L - 1;
+            if (r >= rb && r < rb + Tl)
+                LK(add_launch(rows + (size_t)b * m->D, m->xa + (size_t)r * m->D, pending + (size_t)(r - rb) * m->D,
+                              m->D, m->st));
+        }
+        TRY(allreduce(m, rows, (size_t)batch * m->D));
+        pl = nullptr;
+        ld = m->D;
+        xl = rows;
+    }
     for (int b0 = 0; b0 < batch; b0 += kGemvMaxB) {
         const int nb = std::min(kGemvMaxB, batch - b0);
-        const size_t off = ((size_t)b0 * L + L - 1) * m->D;
-        TRY(lm_head_gemv(m, m->xa + off, (int)ld, pending ? pending + off : nullptr, (int)ld, nb,
+        const size_t off = seq_par ? (size_t)b0 * m->D : ((size_t)b0 * L + L - 1) * m->D;
+        TRY(lm_head_gemv(m, xl + off, (int)ld, pl ? pl + off : nullptr, (int)ld, nb,
                          dlog ? dlog + (size_t)b0 * m->c.vocab : nullptr, m->d_argmax + b0, nullptr, nullptr, 0,
                          nullptr, 0));
     }
@@ -959,6 +1010,8 @@ static qw_status setup_allreduce(qw_model *m) {
     const size_t words = (size_t)m->ar_xoff + (size_t)2 * m->B * m->tp;
     const char *fe = getenv("QW_AR_FUSE");
     m->ar_fuse = !(fe && fe[0] == '0');
+    const char *pe = getenv("QW_PREFILL_SP");
+    m->prefill_sp = !(pe && pe[0] == '0');
     qw_status s = open_peer_buffer(m, words * 8, (void **)&m->ar_buf, m->xch_peer, (void ***)&m->d_ar);
     if (s) return s;
     AL(m->ar_ctr, 2);
